@@ -1,0 +1,192 @@
+/*
+ * techjam_b200.h - C ABI of the B200 (sm_100a) encoder-layer library
+ * (libtechjam_b200.so).
+ *
+ * The library replaces the device work of
+ * `UserOptimizedTransformer.forward(x, valid_token_mask)` in v16_1_clean.py
+ * (v16_1_clean.py:728-735 -> _forward_impl :599-628).  Every entry point takes
+ * plain device pointers, sizes and a CUDA stream (as `void*`, NULL = legacy
+ * default stream), enqueues its kernels on that stream and returns without
+ * synchronising.  No entry point allocates device memory: the caller passes
+ * every buffer, including the workspace sized by tj_encoder_workspace_bytes().
+ *
+ * Return codes: TJ_OK (0) on success, otherwise one of the TJ_ERR_* values;
+ * tj_last_error() then describes the failure (thread-local).  No C++
+ * exception crosses this boundary.
+ *
+ * Device-side failures (a pipeline wait inside a kernel that exceeded its time
+ * limit) are recorded in a per-device status word instead of hanging or
+ * trapping the GPU; tj_device_status() reads and clears it.  With
+ * tj_set_sync_check(1) every entry point synchronises its stream and reports a
+ * recorded device error as TJ_ERR_DEVICE (debugging and tests only).
+ *
+ * Tensor layouts (row-major, innermost last):
+ *   x, out          float32 [B, S, D]
+ *   mask            uint8/bool [B, S], nonzero = valid token (may be NULL)
+ *   weights         float16 [N, K] (nn.Linear layout), biases float32 [N]
+ *   LayerNorm       gamma/beta float32 [D], eps as given (nn.LayerNorm: 1e-5)
+ *   qkv (head-major) float16 [3][H][rows][64]
+ *   ctx             float16 [rows][D]
+ *   "compact rows"  the valid tokens of the batch packed densely in
+ *                   (sample, position) order, as the token plan defines.
+ */
+#ifndef TECHJAM_B200_H_
+#define TECHJAM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TJ_API __attribute__((visibility("default")))
+#else
+#define TJ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TJ_ABI_VERSION 1
+
+#define TJ_OK 0
+#define TJ_ERR_INVALID_ARGUMENT 1
+#define TJ_ERR_UNSUPPORTED 2
+#define TJ_ERR_CUDA 3
+#define TJ_ERR_DEVICE 4
+#define TJ_ERR_WORKSPACE 5
+
+/* ---- library ---------------------------------------------------------- */
+
+/* ABI version (TJ_ABI_VERSION).  No reference counterpart. */
+TJ_API int tj_abi_version(void);
+
+/* Message for the last failed call on this thread ("" if none). */
+TJ_API const char* tj_last_error(void);
+
+/* Copies the message into buf (always NUL-terminated); returns its length. */
+TJ_API int tj_get_last_error(char* buf, size_t len);
+
+/* Enables (1) or disables (0) a stream synchronise + device-status check at
+ * the end of every entry point.  Returns the previous setting. */
+TJ_API int tj_set_sync_check(int enabled);
+
+/* Synchronises `stream`, then copies the current device's status word into
+ * out4 ([0] code, [1] wait site, [2..3] block index; all zero when healthy)
+ * and clears it.  Returns TJ_OK, or TJ_ERR_DEVICE if a device error was
+ * recorded, or TJ_ERR_CUDA if the synchronise itself failed. */
+TJ_API int tj_device_status(int* out4, void* stream);
+
+/* ---- token plan --------------------------------------------------------- */
+
+/* Number of int32 entries tj_token_plan writes for a [B, S] batch. */
+TJ_API int64_t tj_token_plan_ints(int batch, int seq_len);
+
+/* Builds the valid-token plan from `mask` (NULL = every token valid):
+ *   plan[0]                      nv, number of valid tokens
+ *   plan[1 .. B+1]               cu, compact offset of each sample (cu[B] = nv)
+ *   plan[B+2 .. 2B+1]            per-sample valid counts
+ *   plan[2B+2 .. 2B+2+BS)        compact row -> original row b*S+s
+ *   plan[2B+2+BS .. 2B+2+2BS)    original row -> compact row, or -1 if padded
+ * Replaces the mask plumbing of v16_1_clean.py:607-611 (key mask [B,1,1,S] and
+ * query mask [B,S,1]); padded tokens then never enter a GEMM or attention. */
+TJ_API int tj_token_plan(const uint8_t* mask, int batch, int seq_len, int32_t* plan, void* stream);
+
+/* ---- single kernels ------------------------------------------------------ */
+
+/* y16[r] = fp16(LayerNorm(x[row_map ? row_map[r] : r])) for r < min(rows,
+ * *row_count) (row_count may be NULL).  Replaces layer.norm1(x) / norm2(x)
+ * followed by .to(float16): v16_1_clean.py:615-616 + :476, and :527. */
+TJ_API int tj_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* row_count, int rows,
+                   int d_model, const float* gamma, const float* beta, float eps, void* y16,
+                   void* stream);
+
+/* out[m] = LayerNorm(x[inv_map[m]]) for inv_map[m] >= 0, else exact zeros, for
+ * m < rows (inv_map NULL = identity).  Replaces final_norm + masked_fill:
+ * v16_1_clean.py:625-627. */
+TJ_API int tj_ln_final_mask(const float* x, const int32_t* inv_map, int rows, int d_model,
+                     const float* gamma, const float* beta, float eps, float* out, void* stream);
+
+/* qkv16 (head-major [3][H][rows_max][dh]) = fp16(a16 @ w_qkv^T + b_qkv) for the
+ * first min(rows_max, *row_count) rows; w_qkv is the packed [3D, D] q/k/v
+ * weight.  Replaces the packed F.linear + reshape/permute/unbind of
+ * v16_1_clean.py:474-489. */
+TJ_API int tj_gemm_qkv_headmajor(const void* a16, const void* w_qkv16, const float* b_qkv,
+                          const int32_t* row_count, int rows_max, int d_model, int num_heads,
+                          void* qkv16, void* stream);
+
+/* out[r] = a16[r] @ w^T + bias + resid[resid_map ? resid_map[r] : r]  (fp32)
+ * Replaces the fp16 out-projection + .float() + residual add of
+ * v16_1_clean.py:519-523,620 and the FFN-out F.linear + residual of
+ * v16_1_clean.py:533-537,621. */
+TJ_API int tj_gemm_bias_residual_f32(const void* a16, const void* w16, const float* bias,
+                              const float* resid, const int32_t* resid_map,
+                              const int32_t* row_count, int rows_max, int n, int k, float* out,
+                              void* stream);
+
+/* out16[r] = fp16(gelu_erf(a16[r] @ w^T + bias)), GELU evaluated on the fp32
+ * accumulator.  Replaces torch.ops.techjam.v16_1_clean_fused_ffn_gelu_no_preround
+ * (v16_1_clean.py:304-365, Triton kernel :221-301). */
+TJ_API int tj_gemm_bias_gelu_f16(const void* a16, const void* w16, const float* bias,
+                          const int32_t* row_count, int rows_max, int n, int k, void* out16,
+                          void* stream);
+
+/* Masked multi-head attention over compact rows, head_dim 64.
+ *   q16       [H][q_rows][64]
+ *   k16, v16  addressed as [G][H][kv_rows][64] with element strides
+ *             kv_stride_h (between heads) and kv_stride_g (between segments)
+ *   q_cu      [batch+1]: queries of sample b are q rows [q_cu[b], q_cu[b+1])
+ *   kv_off, kv_len [batch*G]: keys of sample b are, for g = 0..G-1 in order,
+ *             rows [kv_off[b*G+g], +kv_len[b*G+g]) of segment g
+ *   ctx16     [q_rows][H*64]: softmax(q k^T * scale) v per head
+ *   causal    mask keys whose position (order within the sample's keys) is
+ *             after the query position q_pos0[b] + (row - q_cu[b]);
+ *             q_pos0 may be NULL (= 0) when G == 1.
+ * Replaces F.scaled_dot_product_attention with the [B,1,1,S] key mask
+ * (v16_1_clean.py:505-514) and the causal branch (:491-504). */
+TJ_API int tj_flash_attn_fwd(const void* q16, const void* k16, const void* v16, int num_heads,
+                      int head_dim, int q_rows, int kv_rows, int64_t kv_stride_h,
+                      int64_t kv_stride_g, int num_segments, int batch, int max_q_per_sample,
+                      const int32_t* q_cu, const int32_t* kv_off, const int32_t* kv_len,
+                      float scale, int causal, const int32_t* q_pos0, void* ctx16, void* stream);
+
+/* ---- whole encoder ----------------------------------------------------- */
+
+typedef struct tj_encoder_desc {
+  int batch, seq_len, d_model, num_heads, ffn_dim, num_layers, causal;
+  float ln_eps;
+} tj_encoder_desc;
+
+typedef struct tj_layer_weights {
+  const float* ln1_gamma;   /* norm1.weight [D] */
+  const float* ln1_beta;    /* norm1.bias [D] */
+  const void* w_qkv16;      /* cat(q,k,v)_proj.weight as fp16 [3D, D] */
+  const float* b_qkv;       /* cat(q,k,v)_proj.bias [3D] */
+  const void* w_out16;      /* attention.out_proj.weight fp16 [D, D] */
+  const float* b_out;       /* [D] */
+  const float* ln2_gamma;   /* norm2.weight */
+  const float* ln2_beta;
+  const void* w_ffn_in16;   /* ffn_in.weight fp16 [F, D] */
+  const float* b_ffn_in;    /* [F] */
+  const void* w_ffn_out16;  /* ffn_out.weight fp16 [D, F] */
+  const float* b_ffn_out;   /* [D] */
+} tj_layer_weights;
+
+/* Workspace bytes tj_encoder_forward needs for this shape (0 on bad shape). */
+TJ_API int64_t tj_encoder_workspace_bytes(const tj_encoder_desc* desc);
+
+/* out = encoder(x, mask): num_layers blocks of
+ *   x = x + out_proj(attn(LN1(x))); x = x + ffn_out(gelu(ffn_in(LN2(x))))
+ * then final LayerNorm, with padded rows exactly zero.  Same arithmetic
+ * contract as UserOptimizedTransformer._forward_impl (v16_1_clean.py:599-628):
+ * fp32 LayerNorm/residual/output, fp16 GEMM operands, fp32 accumulation,
+ * erf-GELU from the fp32 accumulator.  x and out may not alias. */
+TJ_API int tj_encoder_forward(const tj_encoder_desc* desc, const tj_layer_weights* layers,
+                       const float* final_gamma, const float* final_beta, const float* x,
+                       const uint8_t* mask, float* out, void* workspace, int64_t workspace_bytes,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TECHJAM_B200_H_ */

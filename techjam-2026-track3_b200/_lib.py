@@ -1,0 +1,156 @@
+"""ctypes binding of libtechjam_b200.so (the C ABI declared in include/techjam_b200.h).
+
+Only plain pointers, ints and floats cross the boundary; torch tensors are
+unwrapped here with ``data_ptr()`` and the current CUDA stream handle.  A
+missing library or a non-B200 device raises: there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "libtechjam_b200.so"
+
+TJ_OK = 0
+TJ_ERR_INVALID_ARGUMENT = 1
+TJ_ERR_UNSUPPORTED = 2
+TJ_ERR_CUDA = 3
+TJ_ERR_DEVICE = 4
+TJ_ERR_WORKSPACE = 5
+
+_ERR_NAMES = {
+    TJ_ERR_INVALID_ARGUMENT: "invalid argument",
+    TJ_ERR_UNSUPPORTED: "unsupported",
+    TJ_ERR_CUDA: "CUDA error",
+    TJ_ERR_DEVICE: "device error",
+    TJ_ERR_WORKSPACE: "workspace error",
+}
+
+c_int = ctypes.c_int
+c_i64 = ctypes.c_int64
+c_float = ctypes.c_float
+c_vp = ctypes.c_void_p
+
+
+class EncoderDesc(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int),
+        ("seq_len", c_int),
+        ("d_model", c_int),
+        ("num_heads", c_int),
+        ("ffn_dim", c_int),
+        ("num_layers", c_int),
+        ("causal", c_int),
+        ("ln_eps", c_float),
+    ]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [
+        ("ln1_gamma", c_vp),
+        ("ln1_beta", c_vp),
+        ("w_qkv16", c_vp),
+        ("b_qkv", c_vp),
+        ("w_out16", c_vp),
+        ("b_out", c_vp),
+        ("ln2_gamma", c_vp),
+        ("ln2_beta", c_vp),
+        ("w_ffn_in16", c_vp),
+        ("b_ffn_in", c_vp),
+        ("w_ffn_out16", c_vp),
+        ("b_ffn_out", c_vp),
+    ]
+
+
+# name -> (restype, argtypes); every symbol include/techjam_b200.h declares.
+SIGNATURES = {
+    "tj_abi_version": (c_int, []),
+    "tj_last_error": (ctypes.c_char_p, []),
+    "tj_get_last_error": (c_int, [ctypes.c_char_p, ctypes.c_size_t]),
+    "tj_set_sync_check": (c_int, [c_int]),
+    "tj_device_status": (c_int, [ctypes.POINTER(c_int), c_vp]),
+    "tj_token_plan_ints": (c_i64, [c_int, c_int]),
+    "tj_token_plan": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
+    "tj_ln_cast_f16": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
+    "tj_ln_final_mask": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
+    "tj_gemm_qkv_headmajor": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
+    "tj_gemm_bias_residual_f32": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp],
+    ),
+    "tj_gemm_bias_gelu_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
+    "tj_flash_attn_fwd": (
+        c_int,
+        [
+            c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_i64, c_int, c_int, c_int,
+            c_vp, c_vp, c_vp, c_float, c_int, c_vp, c_vp, c_vp,
+        ],
+    ),
+    "tj_encoder_workspace_bytes": (c_i64, [ctypes.POINTER(EncoderDesc)]),
+    "tj_encoder_forward": (
+        c_int,
+        [
+            ctypes.POINTER(EncoderDesc), ctypes.POINTER(LayerWeights), c_vp, c_vp, c_vp, c_vp,
+            c_vp, c_vp, c_i64, c_vp,
+        ],
+    ),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class TJError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, op: str, code: int, message: str) -> None:
+        super().__init__(f"{op}: {_ERR_NAMES.get(code, 'error')} ({code}): {message}")
+        self.op = op
+        self.code = code
+
+
+def load(path: Path | None = None) -> ctypes.CDLL:
+    """Loads the shared library once and declares every entry point."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        lib_path = Path(path) if path is not None else LIB_PATH
+        if not lib_path.exists():
+            raise RuntimeError(
+                f"{lib_path.name} is not built; run `python {PKG_DIR.name}/build.py` "
+                "(or __graft_entry__.build()) first"
+            )
+        lib = ctypes.CDLL(str(lib_path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    msg = load().tj_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, op: str) -> None:
+    if rc != TJ_OK:
+        raise TJError(op, rc, last_error())
+
+
+def set_sync_check(enabled: bool) -> bool:
+    return bool(load().tj_set_sync_check(1 if enabled else 0))
+
+
+def device_status(stream: int = 0) -> list[int]:
+    out = (c_int * 4)()
+    rc = load().tj_device_status(out, c_vp(stream))
+    status = list(out)
+    if rc == TJ_ERR_DEVICE:
+        raise TJError("device_status", rc, last_error())
+    check(rc, "device_status")
+    return status

@@ -1,0 +1,409 @@
+// Persistent tcgen05 GEMM, C[M,N] = A[M,K] * W[N,K]^T with fp16 operands and an
+// fp32 TMEM accumulator, and the three epilogues the encoder layer needs:
+//
+//   kEpiQkvHeadMajor  QKV projection (v16_1_clean.py:474-489): +bias, fp16,
+//                     stored straight into the head-major [3][H][rows][dh]
+//                     layout attention reads, so no permute/contiguous pass.
+//   kEpiResidualF32   output projection (v16_1_clean.py:516-523 + :620) and
+//                     FFN-out (v16_1_clean.py:533-537 + :621): +bias, +fp32
+//                     residual, fp32 store.
+//   kEpiGeluF16       FFN-in (v16_1_clean.py:221-301, the Triton fused op):
+//                     +bias, exact erf-GELU on the fp32 accumulator, fp16.
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
+//               shared-memory stages, completion on mbarriers.
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128, N=BN,
+//               K=16 per instruction) into one of two TMEM accumulators.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)..+31 = tile rows), fused math, global stores.
+// Two accumulators let the epilogue of tile i overlap the main loop of tile
+// i+1.  Tiles are walked n-fastest so CTAs running at the same time share the
+// A tile through L2.  The number of rows comes from device memory (the token
+// plan), so the host never synchronises to learn it.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace tj {
+
+constexpr int kGemmThreads = 192;
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+
+struct GemmKernelParams {
+  const float* bias;
+  const int32_t* row_count;
+  int rows_max, N, K;
+  void* out;
+  int ld_out;
+  const float* resid;
+  const int32_t* resid_map;
+  int ld_resid;
+  int heads, head_dim, d_model;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+  static constexpr size_t kSmemBytes =
+      1024 /*align slack*/ + (size_t)kStages * kStageBytes + 256 /*barriers etc*/;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+// Wait without the CTA abort flag: used on the exit path to let TMA loads or
+// MMAs already in flight land before the CTA releases its shared memory/TMEM.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmKernelParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+  // bars: full[S], empty[S], tfull[2], tempty[2], final
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_idx();
+  const uint32_t lane = lane_id();
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + S + s); };
+  auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * S + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * S + 2 + a); };
+  const uint32_t final_bar = smem_u32(bars + 2 * S + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = device_failed() ? 1 : 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int rows = p.row_count ? min(p.rows_max, *p.row_count) : p.rows_max;
+  const int m_tiles = (rows + kBM - 1) / kBM;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int total_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_parity[S];
+      for (int s = 0; s < S; ++s) last_parity[s] = -1;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t / n_tiles) * kBM;
+        const int n0 = (t % n_tiles) * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, 100 + EPI)) break;
+          mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
+          tma_load_2d(smem_u32(sA + stage * Cfg::kABytes), &tmA, full_bar(stage), kb * kBK, m0);
+          tma_load_2d(smem_u32(sB + stage * Cfg::kBBytes), &tmB, full_bar(stage), kb * kBK, n0);
+          last_parity[stage] = (int)phase;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Let every issued load land before the CTA can exit.
+      for (int s = 0; s < S; ++s)
+        if (last_parity[s] >= 0) drain_wait(full_bar(s), (uint32_t)last_parity[s]);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued = false;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, abort_flag, 110 + EPI)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, 120 + EPI)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a_desc = sw128_desc(smem_u32(sA + stage * Cfg::kABytes), 16, 1024);
+          const uint64_t b_desc = sw128_desc(smem_u32(sB + stage * Cfg::kBBytes), 16, 1024);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes per K=16 step inside the 128-byte swizzled row.
+            mma_f16_ss(d_tmem, a_desc + (uint64_t)(2 * k), b_desc + (uint64_t)(2 * k), idesc,
+                       (kb | k) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit(empty_bar(stage));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(tfull_bar(acc));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (issued) {
+        mma_commit(final_bar);
+        drain_wait(final_bar, 0);
+      }
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + (int)lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+      const int m0 = (t / n_tiles) * kBM;
+      const int n0 = (t % n_tiles) * BN;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, 130 + EPI)) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < rows;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      int64_t resid_row = 0;
+      if (EPI == kEpiResidualF32 && row_ok)
+        resid_row = p.resid_map ? (int64_t)p.resid_map[row] : (int64_t)row;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + (uint32_t)(c * 32), r);
+        tmem_ld_wait();
+        const int nc = n0 + c * 32;
+        if (!row_ok || nc >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int n = nc + 8 * g;
+          if (n >= p.N) break;
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + n) + 1);
+          float w[8] = {v[8 * g + 0] + b0.x, v[8 * g + 1] + b0.y, v[8 * g + 2] + b0.z,
+                        v[8 * g + 3] + b0.w, v[8 * g + 4] + b1.x, v[8 * g + 5] + b1.y,
+                        v[8 * g + 6] + b1.z, v[8 * g + 7] + b1.w};
+          if (EPI == kEpiQkvHeadMajor) {
+            const int which = n / p.d_model;
+            const int rem = n - which * p.d_model;
+            const int h = rem / p.head_dim;
+            const int d = rem - h * p.head_dim;
+            __half* dst = static_cast<__half*>(p.out) +
+                          (((int64_t)(which * p.heads + h) * p.rows_max + row) * p.head_dim + d);
+            uint4 o;
+            o.x = pack_half2(w[0], w[1]);
+            o.y = pack_half2(w[2], w[3]);
+            o.z = pack_half2(w[4], w[5]);
+            o.w = pack_half2(w[6], w[7]);
+            *reinterpret_cast<uint4*>(dst) = o;
+          } else if (EPI == kEpiGeluF16) {
+            __half* dst = static_cast<__half*>(p.out) + (int64_t)row * p.ld_out + n;
+            uint4 o;
+            o.x = pack_half2(gelu_erf(w[0]), gelu_erf(w[1]));
+            o.y = pack_half2(gelu_erf(w[2]), gelu_erf(w[3]));
+            o.z = pack_half2(gelu_erf(w[4]), gelu_erf(w[5]));
+            o.w = pack_half2(gelu_erf(w[6]), gelu_erf(w[7]));
+            *reinterpret_cast<uint4*>(dst) = o;
+          } else {
+            const float4* rs =
+                reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + n);
+            const float4 r0 = __ldg(rs), r1 = __ldg(rs + 1);
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                    (int64_t)row * p.ld_out + n);
+            dst[0] = make_float4(w[0] + r0.x, w[1] + r0.y, w[2] + r0.z, w[3] + r0.w);
+            dst[1] = make_float4(w[4] + r1.x, w[5] + r1.y, w[6] + r1.z, w[7] + r1.w);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// fp16 tensor map of rank 2..5 with a 128-byte swizzle.  dims/strides are in
+// elements, innermost first; strides has rank-1 entries (dims 1..rank-1).
+int make_tmap_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides_elems, const uint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(TJ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estride[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) gstride[i] = strides_elems[i] * 2;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
+                  gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d) rank=%d", (int)r,
+                     rank);
+  return TJ_OK;
+}
+
+template <int BN, int EPI>
+static int launch_gemm_t(const GemmArgs& a, const GemmKernelParams& kp, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  uint64_t da[2] = {(uint64_t)a.K, (uint64_t)a.rows_max};
+  uint64_t sa[1] = {(uint64_t)a.K};
+  uint32_t ba[2] = {kBK, kBM};
+  int rc = make_tmap_f16(&ta, a.a16, 2, da, sa, ba);
+  if (rc) return rc;
+  uint64_t db[2] = {(uint64_t)a.K, (uint64_t)a.N};
+  uint64_t sb[1] = {(uint64_t)a.K};
+  uint32_t bb[2] = {kBK, (uint32_t)BN};
+  rc = make_tmap_f16(&tb, a.w16, 2, db, sb, bb);
+  if (rc) return rc;
+
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::kSmemBytes);
+    if (e != cudaSuccess)
+      return set_error(TJ_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
+    attr_set = true;
+  }
+  int num_sms = 0;
+  rc = ensure_device_props(&num_sms);
+  if (rc) return rc;
+  const int max_tiles = ((a.rows_max + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
+  const int grid = max_tiles < num_sms ? max_tiles : num_sms;
+  if (grid <= 0) return TJ_OK;
+  gemm_tcgen05_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+  return TJ_OK;
+}
+
+int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
+  if (a.rows_max < 0 || a.N <= 0 || a.K <= 0)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: rows=%d N=%d K=%d", a.rows_max, a.N, a.K);
+  if (a.K % 8 != 0 || a.N % 8 != 0)
+    return set_error(TJ_ERR_UNSUPPORTED, "gemm: N=%d and K=%d must be multiples of 8", a.N, a.K);
+  if (!a.a16 || !a.w16 || !a.bias || !a.out)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: null pointer");
+  if ((reinterpret_cast<uintptr_t>(a.a16) | reinterpret_cast<uintptr_t>(a.w16) |
+       reinterpret_cast<uintptr_t>(a.bias) | reinterpret_cast<uintptr_t>(a.out)) & 15u)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: operands must be 16-byte aligned");
+  if (a.rows_max == 0) return TJ_OK;
+  GemmKernelParams kp{};
+  kp.bias = a.bias;
+  kp.row_count = a.row_count;
+  kp.rows_max = a.rows_max;
+  kp.N = a.N;
+  kp.K = a.K;
+  kp.out = a.out;
+  kp.ld_out = a.ld_out;
+  kp.resid = a.resid;
+  kp.resid_map = a.resid_map;
+  kp.ld_resid = a.ld_resid;
+  kp.heads = a.heads;
+  kp.head_dim = a.head_dim;
+  switch (epilogue) {
+    case kEpiQkvHeadMajor:
+      if (a.heads <= 0 || a.head_dim <= 0 || a.head_dim % 8 != 0 || a.N != 3 * a.heads * a.head_dim)
+        return set_error(TJ_ERR_UNSUPPORTED,
+                         "gemm_qkv_headmajor: N=%d must be 3*H*dh with dh %% 8 == 0 (H=%d dh=%d)",
+                         a.N, a.heads, a.head_dim);
+      kp.d_model = a.heads * a.head_dim;
+      return launch_gemm_t<256, kEpiQkvHeadMajor>(a, kp, stream);
+    case kEpiResidualF32:
+      if (!a.resid || (reinterpret_cast<uintptr_t>(a.resid) & 15u) || a.ld_resid % 4 != 0 ||
+          a.ld_out % 4 != 0)
+        return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_residual_f32: residual must be 16-byte aligned");
+      return launch_gemm_t<256, kEpiResidualF32>(a, kp, stream);
+    case kEpiGeluF16:
+      if (a.ld_out % 8 != 0)
+        return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_gelu_f16: ld_out must be a multiple of 8");
+      return launch_gemm_t<256, kEpiGeluF16>(a, kp, stream);
+    default:
+      return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epilogue);
+  }
+}
+
+}  // namespace tj

@@ -1,0 +1,92 @@
+// Host-side launchers shared between the kernel files and the C-ABI layer.
+// Every launcher checks its own arguments and returns a tj status code
+// (TJ_OK on success); none of them synchronises or allocates.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/techjam_b200.h"
+
+namespace tj {
+
+// Records a printf-style message for tj_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+int ensure_device_props(int* num_sms);
+
+// Number of int32 entries of the token plan for a [B, S] batch.
+int64_t plan_ints(int B, int S);
+
+// Token plan layout (int32):
+//   [0]                 nv  (number of valid tokens)
+//   [1, 1+B+1)          cu  (compact offset of each sample; cu[B] = nv)
+//   [B+2, B+2+B)        n   (valid tokens per sample)
+//   [2B+2, 2B+2+BS)     orig (compact row -> original row b*S+s)
+//   [2B+2+BS, ...+BS)   inv  (original row -> compact row, or -1)
+struct PlanView {
+  int32_t* base;
+  int B, S;
+  int32_t* nv() const { return base; }
+  int32_t* cu() const { return base + 1; }
+  int32_t* n() const { return base + 2 + B; }
+  int32_t* orig() const { return base + 2 + 2 * B; }
+  int32_t* inv() const { return base + 2 + 2 * B + (int64_t)B * S; }
+};
+
+int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStream_t stream);
+
+int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* row_count, int rows,
+                       int D, const float* gamma, const float* beta, float eps, void* y16,
+                       cudaStream_t stream);
+
+int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
+                    const float* beta, float eps, float* out, cudaStream_t stream);
+
+enum GemmEpilogue : int {
+  kEpiQkvHeadMajor = 0,   // fp16 out, head-major [3][H][rows_max][dh]
+  kEpiResidualF32 = 1,    // fp32 out = acc + bias + residual[row_map(row)]
+  kEpiGeluF16 = 2,        // fp16 out = gelu_erf(acc + bias)
+};
+
+struct GemmArgs {
+  const void* a16;          // [rows_max, K] fp16, row-major
+  const void* w16;          // [N, K] fp16, row-major (nn.Linear layout)
+  const float* bias;        // [N]
+  const int32_t* row_count; // device int (rows actually present), or null = rows_max
+  int rows_max, N, K;
+  void* out;                // epilogue-dependent
+  int ld_out;               // elements
+  const float* resid;       // kEpiResidualF32
+  const int32_t* resid_map; // optional gather map for residual rows
+  int ld_resid;
+  int heads, head_dim;      // kEpiQkvHeadMajor
+};
+
+int launch_gemm(int epilogue, const GemmArgs& args, cudaStream_t stream);
+
+struct AttnArgs {
+  const void* q;            // fp16 [H][q_rows][dh]
+  const void* k;            // fp16, addressed as [G][H][kv_rows][dh] with strides below
+  const void* v;
+  int H, head_dim;
+  int q_rows;               // rows of the Q slab per head
+  int kv_rows;              // rows of one K/V slab per head and segment
+  int64_t kv_stride_h;      // elements between heads
+  int64_t kv_stride_g;      // elements between segments
+  int G;                    // key segments per sample
+  int B;                    // samples
+  int max_q_per_sample;     // upper bound on valid queries per sample
+  const int32_t* q_cu;      // [B+1] compact query offsets
+  const int32_t* kv_off;    // [B*G] row offset of each key segment
+  const int32_t* kv_len;    // [B*G] keys in each segment
+  int64_t kv_len_stride;    // stride between samples in kv_off/kv_len (usually G)
+  float scale;              // softmax scale (head_dim^-0.5)
+  int causal;               // 1: key position > query position masked
+  const int32_t* q_pos0;    // causal only: position of the first query of each sample
+  void* ctx;                // fp16 [q_rows][H*dh]
+};
+
+int launch_attention(const AttnArgs& args, cudaStream_t stream);
+
+}  // namespace tj

@@ -1,0 +1,282 @@
+// Token plan (valid-token compaction) and the two LayerNorm kernels.
+//
+// The reference masks padded keys inside attention and zeroes padded rows
+// after the block and after the final LayerNorm
+// (torch_transformer_benchmark.py:105-108,143-144,169-171).  Rows are
+// independent everywhere except in attention, where a padded key only ever
+// contributes exp(-inf) = 0.  So the whole layer can run on the valid tokens
+// alone, packed densely: the token plan maps each valid token to a compact row
+// (and back), the GEMMs and attention see only compact rows, and the final
+// LayerNorm scatters back to [B, S, D] writing exact zeros for padded rows.
+//
+// LayerNorm follows nn.LayerNorm (biased variance, eps inside the rsqrt) as
+// used at torch_transformer_benchmark.py:128-130,160 and
+// v16_1_clean.py:615,527,625.  HBM-bound: one warp per row, the row kept in
+// registers between the mean and the variance pass.
+#include <stdarg.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace tj {
+
+// ---------------------------------------------------------------------------
+// Token plan: one CTA of 1024 threads.  Thread t owns a contiguous chunk of
+// the B*S mask bytes; a block-wide exclusive scan of the per-chunk valid
+// counts gives each chunk its first compact row.
+// ---------------------------------------------------------------------------
+constexpr int kPlanThreads = 1024;
+
+__global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t* __restrict__ mask,
+                                                                  int B, int S,
+                                                                  int32_t* __restrict__ plan) {
+  const int64_t total = (int64_t)B * S;
+  const int64_t chunk = (total + kPlanThreads - 1) / kPlanThreads;
+  const int64_t begin = min(total, (int64_t)threadIdx.x * chunk);
+  const int64_t end = min(total, begin + chunk);
+
+  int32_t* cu = plan + 1;
+  int32_t* cnt = plan + 2 + B;
+  int32_t* orig = plan + 2 + 2 * B;
+  int32_t* inv = orig + total;
+
+  int count = 0;
+  if (mask == nullptr) {
+    count = (int)(end - begin);
+  } else {
+    for (int64_t i = begin; i < end; ++i) count += mask[i] != 0;
+  }
+
+  // Block exclusive scan (warp shuffles, then a scan of the 32 warp totals).
+  __shared__ int warp_tot[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = count;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_tot[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
+    }
+    warp_tot[lane] = wi - w;  // exclusive prefix of warp totals
+  }
+  __syncthreads();
+  int run = warp_tot[warp] + incl - count;
+
+  for (int64_t i = begin; i < end; ++i) {
+    if (i % S == 0) cu[i / S] = run;
+    const bool valid = (mask == nullptr) || mask[i] != 0;
+    if (valid) {
+      orig[run] = (int32_t)i;
+      inv[i] = run;
+      ++run;
+    } else {
+      inv[i] = -1;
+    }
+  }
+  // The thread owning the last element publishes the total.
+  if (end == total && begin < end) {
+    cu[B] = run;
+    plan[0] = run;
+  }
+  if (total == 0 && threadIdx.x == 0) {
+    cu[B] = 0;
+    plan[0] = 0;
+  }
+  __syncthreads();
+  __threadfence_block();
+  for (int b = threadIdx.x; b < B; b += kPlanThreads) {
+    cnt[b] = ((volatile int32_t*)cu)[b + 1] - ((volatile int32_t*)cu)[b];
+  }
+}
+
+int64_t plan_ints(int B, int S) { return 2 + 2 * (int64_t)B + 2 * (int64_t)B * S; }
+
+int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStream_t stream) {
+  if (B <= 0 || S <= 0) return set_error(TJ_ERR_INVALID_ARGUMENT, "token_plan: B=%d S=%d", B, S);
+  if ((int64_t)B * S > (int64_t)INT32_MAX - 1)
+    return set_error(TJ_ERR_UNSUPPORTED, "token_plan: B*S=%lld exceeds int32", (long long)B * S);
+  if (plan == nullptr) return set_error(TJ_ERR_INVALID_ARGUMENT, "token_plan: null plan buffer");
+  token_plan_kernel<<<1, kPlanThreads, 0, stream>>>(mask, B, S, plan);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "token_plan launch: %s", cudaGetErrorString(e));
+  return TJ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm.  One warp per row; lane l holds float4 groups l, l+32, ... of the
+// row (VPL groups per lane, so D <= 128 * VPL).
+// ---------------------------------------------------------------------------
+template <int VPL>
+__device__ __forceinline__ void ln_row_stats(const float4 (&v)[VPL], int D, int lane, float& mean,
+                                             float& rstd, float eps) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    if ((i * 32 + lane) * 4 < D) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  mean = s / (float)D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    if ((i * 32 + lane) * 4 < D) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  rstd = 1.0f / sqrtf(q / (float)D + eps);
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) ln_cast_f16_kernel(
+    const float* __restrict__ x, const int32_t* __restrict__ row_map,
+    const int32_t* __restrict__ row_count, int rows, int D, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float eps, __half* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int limit = row_count ? min(rows, *row_count) : rows;
+  if (row >= limit) return;
+  const int64_t src = row_map ? (int64_t)row_map[row] : (int64_t)row;
+  const float4* xr = reinterpret_cast<const float4*>(x + src * D);
+  float4 v[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int g = i * 32 + lane;
+    v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean, rstd;
+  ln_row_stats<VPL>(v, D, lane, mean, rstd, eps);
+  uint2* yr = reinterpret_cast<uint2*>(y + (int64_t)row * D);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int g = i * 32 + lane;
+    if (g * 4 < D) {
+      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma) + g);
+      const float4 be = __ldg(reinterpret_cast<const float4*>(beta) + g);
+      uint2 o;
+      o.x = pack_half2((v[i].x - mean) * rstd * ga.x + be.x, (v[i].y - mean) * rstd * ga.y + be.y);
+      o.y = pack_half2((v[i].z - mean) * rstd * ga.z + be.z, (v[i].w - mean) * rstd * ga.w + be.w);
+      yr[g] = o;
+    }
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__ x,
+                                                       const int32_t* __restrict__ inv_map,
+                                                       int rows, int D,
+                                                       const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta, float eps,
+                                                       float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t src = inv_map ? (int64_t)inv_map[row] : (int64_t)row;
+  float4* orow = reinterpret_cast<float4*>(out + (int64_t)row * D);
+  if (src < 0) {  // padded token: exact zero, as masked_fill(~mask, 0) gives
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int g = i * 32 + lane;
+      if (g * 4 < D) orow[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    return;
+  }
+  const float4* xr = reinterpret_cast<const float4*>(x + src * D);
+  float4 v[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int g = i * 32 + lane;
+    v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean, rstd;
+  ln_row_stats<VPL>(v, D, lane, mean, rstd, eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int g = i * 32 + lane;
+    if (g * 4 < D) {
+      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma) + g);
+      const float4 be = __ldg(reinterpret_cast<const float4*>(beta) + g);
+      float4 o;
+      o.x = (v[i].x - mean) * rstd * ga.x + be.x;
+      o.y = (v[i].y - mean) * rstd * ga.y + be.y;
+      o.z = (v[i].z - mean) * rstd * ga.z + be.z;
+      o.w = (v[i].w - mean) * rstd * ga.w + be.w;
+      orow[g] = o;
+    }
+  }
+}
+
+static int ln_vpl(int D) {
+  const int groups = (D / 4 + 31) / 32;
+  if (groups <= 1) return 1;
+  if (groups <= 2) return 2;
+  if (groups <= 4) return 4;
+  if (groups <= 8) return 8;
+  if (groups <= 16) return 16;
+  if (groups <= 32) return 32;
+  return -1;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* row_count, int rows,
+                       int D, const float* gamma, const float* beta, float eps, void* y16,
+                       cudaStream_t stream) {
+  if (rows < 0 || D <= 0 || D % 4 != 0)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
+  const int vpl = ln_vpl(D);
+  if (vpl < 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_cast_f16: D=%d above 4096", D);
+  if (!x || !gamma || !beta || !y16 || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
+      (reinterpret_cast<uintptr_t>(y16) & 7u))
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: null or misaligned pointer");
+  if (rows == 0) return TJ_OK;
+  const int warps = 8;
+  dim3 grid((rows + warps - 1) / warps);
+  __half* y = static_cast<__half*>(y16);
+  switch (vpl) {
+#define TJ_LN_CASE(V) \
+  case V: ln_cast_f16_kernel<V><<<grid, warps * 32, 0, stream>>>(x, row_map, row_count, rows, D, gamma, beta, eps, y); break;
+    TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
+#undef TJ_LN_CASE
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_cast_f16 launch: %s", cudaGetErrorString(e));
+  return TJ_OK;
+}
+
+int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
+                    const float* beta, float eps, float* out, cudaStream_t stream) {
+  if (rows < 0 || D <= 0 || D % 4 != 0)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
+  const int vpl = ln_vpl(D);
+  if (vpl < 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_final_mask: D=%d above 4096", D);
+  if (!x || !gamma || !beta || !out || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
+      !aligned16(out))
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: null or misaligned pointer");
+  if (rows == 0) return TJ_OK;
+  const int warps = 8;
+  dim3 grid((rows + warps - 1) / warps);
+  switch (vpl) {
+#define TJ_LN_CASE(V) \
+  case V: ln_final_kernel<V><<<grid, warps * 32, 0, stream>>>(x, inv_map, rows, D, gamma, beta, eps, out); break;
+    TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
+#undef TJ_LN_CASE
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_final_mask launch: %s", cudaGetErrorString(e));
+  return TJ_OK;
+}
+
+}  // namespace tj

@@ -1,0 +1,186 @@
+"""Torch-facing wrappers of the single-kernel C-ABI entry points.
+
+Each wrapper validates device, dtype, contiguity and shape the way the
+reference's custom op does (v16_1_clean.py:323-335: TypeError/ValueError on
+bad inputs), then passes raw pointers and the current CUDA stream to the
+library.  They exist for the per-kernel parity tests and for callers that
+compose the layer themselves; UserOptimizedTransformer uses the single
+tj_encoder_forward entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require(t: torch.Tensor, name: str, dtype: torch.dtype, device: torch.device) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.device != device:
+        raise ValueError(f"{name} must be on {device}, got {t.device}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def token_plan(mask: Optional[torch.Tensor], batch: int, seq_len: int, device) -> torch.Tensor:
+    lib = _lib.load()
+    n = lib.tj_token_plan_ints(batch, seq_len)
+    plan = torch.empty(n, dtype=torch.int32, device=device)
+    mptr = None
+    if mask is not None:
+        if mask.shape != (batch, seq_len):
+            raise ValueError(f"mask must be [{batch}, {seq_len}], got {tuple(mask.shape)}")
+        m = mask.contiguous()
+        if m.dtype == torch.bool:
+            m = m.view(torch.uint8)
+        _require(m, "mask", torch.uint8, plan.device)
+        mptr = m.data_ptr()
+    _lib.check(lib.tj_token_plan(mptr, batch, seq_len, plan.data_ptr(), _stream(plan)), "token_plan")
+    return plan
+
+
+def plan_views(plan: torch.Tensor, batch: int, seq_len: int):
+    """(nv[1], cu[B+1], counts[B], orig[BS], inv[BS]) views of a token plan."""
+    B, BS = batch, batch * seq_len
+    nv = plan[0:1]
+    cu = plan[1 : B + 2]
+    cnt = plan[B + 2 : 2 * B + 2]
+    orig = plan[2 * B + 2 : 2 * B + 2 + BS]
+    inv = plan[2 * B + 2 + BS : 2 * B + 2 + 2 * BS]
+    return nv, cu, cnt, orig, inv
+
+
+def ln_cast_f16(x, gamma, beta, eps=1e-5, row_map=None, row_count=None, out=None):
+    dev = x.device
+    _require(x, "x", torch.float32, dev)
+    D = x.shape[-1]
+    rows = x.numel() // D if row_map is None else row_map.numel()
+    if out is None:
+        out = torch.empty(rows, D, dtype=torch.float16, device=dev)
+    lib = _lib.load()
+    rc = lib.tj_ln_cast_f16(
+        x.data_ptr(), _ptr(row_map), _ptr(row_count), rows, D, gamma.data_ptr(), beta.data_ptr(),
+        float(eps), out.data_ptr(), _stream(x),
+    )
+    _lib.check(rc, "ln_cast_f16")
+    return out
+
+
+def ln_final_mask(x, gamma, beta, eps=1e-5, inv_map=None, rows=None, out=None):
+    dev = x.device
+    _require(x, "x", torch.float32, dev)
+    D = x.shape[-1]
+    if rows is None:
+        rows = x.numel() // D if inv_map is None else inv_map.numel()
+    if out is None:
+        out = torch.empty(rows, D, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    rc = lib.tj_ln_final_mask(
+        x.data_ptr(), _ptr(inv_map), rows, D, gamma.data_ptr(), beta.data_ptr(), float(eps),
+        out.data_ptr(), _stream(x),
+    )
+    _lib.check(rc, "ln_final_mask")
+    return out
+
+
+def gemm_qkv_headmajor(a16, w_qkv16, b_qkv, num_heads, row_count=None, out=None):
+    dev = a16.device
+    _require(a16, "a16", torch.float16, dev)
+    _require(w_qkv16, "w_qkv16", torch.float16, dev)
+    _require(b_qkv, "b_qkv", torch.float32, dev)
+    rows, D = a16.shape
+    if w_qkv16.shape != (3 * D, D):
+        raise ValueError(f"w_qkv16 must be [{3 * D}, {D}], got {tuple(w_qkv16.shape)}")
+    dh = D // num_heads
+    if out is None:
+        out = torch.empty(3, num_heads, rows, dh, dtype=torch.float16, device=dev)
+    lib = _lib.load()
+    rc = lib.tj_gemm_qkv_headmajor(
+        a16.data_ptr(), w_qkv16.data_ptr(), b_qkv.data_ptr(), _ptr(row_count), rows, D, num_heads,
+        out.data_ptr(), _stream(a16),
+    )
+    _lib.check(rc, "gemm_qkv_headmajor")
+    return out
+
+
+def gemm_bias_residual_f32(a16, w16, bias, resid, resid_map=None, row_count=None, out=None):
+    dev = a16.device
+    _require(a16, "a16", torch.float16, dev)
+    _require(w16, "w16", torch.float16, dev)
+    _require(bias, "bias", torch.float32, dev)
+    _require(resid, "resid", torch.float32, dev)
+    rows, K = a16.shape
+    N = w16.shape[0]
+    if w16.shape[1] != K:
+        raise ValueError("w16 inner dimension does not match a16")
+    if out is None:
+        out = torch.empty(rows, N, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    rc = lib.tj_gemm_bias_residual_f32(
+        a16.data_ptr(), w16.data_ptr(), bias.data_ptr(), resid.data_ptr(), _ptr(resid_map),
+        _ptr(row_count), rows, N, K, out.data_ptr(), _stream(a16),
+    )
+    _lib.check(rc, "gemm_bias_residual_f32")
+    return out
+
+
+def gemm_bias_gelu_f16(a16, w16, bias, row_count=None, out=None):
+    dev = a16.device
+    _require(a16, "a16", torch.float16, dev)
+    _require(w16, "w16", torch.float16, dev)
+    _require(bias, "bias", torch.float32, dev)
+    rows, K = a16.shape
+    N = w16.shape[0]
+    if w16.shape[1] != K:
+        raise ValueError("w16 inner dimension does not match a16")
+    if out is None:
+        out = torch.empty(rows, N, dtype=torch.float16, device=dev)
+    lib = _lib.load()
+    rc = lib.tj_gemm_bias_gelu_f16(
+        a16.data_ptr(), w16.data_ptr(), bias.data_ptr(), _ptr(row_count), rows, N, K,
+        out.data_ptr(), _stream(a16),
+    )
+    _lib.check(rc, "gemm_bias_gelu_f16")
+    return out
+
+
+def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causal=False,
+                   q_pos0=None, out=None):
+    """q: [H, q_rows, 64]; k, v: [G, H, kv_rows, 64] (any strides with unit inner stride);
+    q_cu: [B+1]; kv_off/kv_len: [B, G] int32.  Returns ctx [q_rows, H*64] fp16."""
+    dev = q.device
+    _require(q, "q", torch.float16, dev)
+    if k.dim() == 3:
+        k = k.unsqueeze(0)
+        v = v.unsqueeze(0)
+    G, H, kv_rows, dh = k.shape
+    if q.shape[0] != H or q.shape[2] != dh:
+        raise ValueError("q must be [H, q_rows, head_dim] matching k")
+    if k.stride() != v.stride() or k.stride(-1) != 1 or k.stride(-2) != dh:
+        raise ValueError("k and v must share strides with contiguous [rows, head_dim] slabs")
+    B = q_cu.numel() - 1
+    if out is None:
+        out = torch.empty(q.shape[1], H * dh, dtype=torch.float16, device=dev)
+    lib = _lib.load()
+    rc = lib.tj_flash_attn_fwd(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), H, dh, q.shape[1], kv_rows, k.stride(1),
+        k.stride(0), G, B, max_q_per_sample, q_cu.data_ptr(), kv_off.data_ptr(),
+        kv_len.data_ptr(), float(scale), 1 if causal else 0, _ptr(q_pos0), out.data_ptr(),
+        _stream(q),
+    )
+    _lib.check(rc, "flash_attn_fwd")
+    return out

@@ -1,0 +1,209 @@
+"""Per-kernel parity on the B200, through the C ABI (kernels.py -> ctypes).
+
+Each kernel is compared with a plain PyTorch FP32 (or float64) computation of
+the same op on the same fp16 operands; tolerances are written per test.
+"""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _sync_check(cuda_pkg):
+    prev = cuda_pkg._lib.set_sync_check(True)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    cuda_pkg._lib.set_sync_check(prev)
+
+
+def _plan_reference(mask):
+    B, S = mask.shape
+    flat = mask.reshape(-1).bool()
+    orig = torch.nonzero(flat).flatten().int()
+    inv = torch.full((B * S,), -1, dtype=torch.int32)
+    inv[orig.long()] = torch.arange(orig.numel(), dtype=torch.int32)
+    counts = mask.sum(1).int()
+    cu = torch.zeros(B + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(counts, 0)
+    return orig, inv, counts, cu
+
+
+@pytest.mark.parametrize("B,S", [(1, 1), (2, 8), (3, 1000), (8, 2048), (1, 131072)])
+def test_token_plan(cuda_pkg, B, S):
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(B * 7 + S)
+    lengths = torch.randint(0, S + 1, (B,), generator=g)
+    mask = torch.arange(S)[None, :] < lengths[:, None]
+    if B >= 3:
+        mask[1] = torch.rand(S, generator=g) < 0.3  # a non-prefix row
+        mask[0] = False  # an all-padded row
+    plan = k.token_plan(mask.to(DEV), B, S, DEV)
+    nv, cu, cnt, orig, inv = [t.cpu() for t in k.plan_views(plan, B, S)]
+    r_orig, r_inv, r_cnt, r_cu = _plan_reference(mask)
+    assert int(nv) == int(mask.sum())
+    assert torch.equal(cu, r_cu)
+    assert torch.equal(cnt, r_cnt)
+    assert torch.equal(orig[: int(nv)], r_orig)
+    assert torch.equal(inv, r_inv)
+    # No mask: identity plan.
+    plan = k.token_plan(None, B, S, DEV)
+    nv, cu, cnt, orig, inv = [t.cpu() for t in k.plan_views(plan, B, S)]
+    assert int(nv) == B * S
+    assert torch.equal(orig, torch.arange(B * S, dtype=torch.int32))
+
+
+@pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (1000, 768), (513, 1024), (64, 4096)])
+def test_ln_cast_and_final(cuda_pkg, rows, D):
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(rows + D)
+    x = torch.randn(rows, D, generator=g) * 3 + 0.5
+    gamma = 1 + 0.1 * torch.randn(D, generator=g)
+    beta = 0.1 * torch.randn(D, generator=g)
+    ref = torch.nn.functional.layer_norm(x.double(), (D,), gamma.double(), beta.double(), 1e-5)
+    xd, gd, bd = x.to(DEV), gamma.to(DEV), beta.to(DEV)
+    y16 = k.ln_cast_f16(xd, gd, bd).cpu().double()
+    # fp16 rounding of the fp32 result: <= 1 ulp of fp16 (2^-10 relative) plus fp32 noise.
+    assert torch.all((y16 - ref).abs() <= ref.abs() * 2**-10 + 1e-5)
+    # gather map + row count
+    perm = torch.randperm(rows, generator=g).int()
+    cnt = torch.tensor([rows // 2], dtype=torch.int32)
+    y16m = k.ln_cast_f16(xd, gd, bd, row_map=perm.to(DEV), row_count=cnt.to(DEV)).cpu().double()
+    half = rows // 2
+    refm = ref[perm.long()[:half]]
+    assert torch.all((y16m[:half] - refm).abs() <= refm.abs() * 2**-10 + 1e-5)
+    # final LN with inverse map and padded rows
+    inv = torch.arange(rows, dtype=torch.int32)
+    inv[::3] = -1
+    out = k.ln_final_mask(xd, gd, bd, inv_map=inv.to(DEV)).cpu().double()
+    valid = inv >= 0
+    torch.testing.assert_close(out[valid], ref[valid], rtol=0, atol=2e-5)
+    assert torch.count_nonzero(out[~valid]) == 0
+
+
+def _gemm_ref(a16, w16, bias):
+    return a16.float() @ w16.float().t() + bias
+
+
+@pytest.mark.parametrize("rows,count,D,H", [(128, 128, 256, 4), (1000, 777, 768, 12), (4096, 4096, 1024, 16), (300, 0, 256, 4)])
+def test_gemm_qkv_headmajor(cuda_pkg, rows, count, D, H):
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(rows + D)
+    a = torch.randn(rows, D, generator=g).half().to(DEV)
+    w = (torch.randn(3 * D, D, generator=g) / math.sqrt(D)).half().to(DEV)
+    b = torch.randn(3 * D, generator=g).to(DEV)
+    out = torch.full((3, H, rows, D // H), float("nan"), dtype=torch.float16, device=DEV)
+    k.gemm_qkv_headmajor(a, w, b, H, row_count=torch.tensor([count], dtype=torch.int32, device=DEV), out=out)
+    ref = _gemm_ref(a, w, b)  # [rows, 3D]
+    ref_hm = ref.view(rows, 3, H, D // H).permute(1, 2, 0, 3)
+    got = out[:, :, :count].float()
+    exp = ref_hm[:, :, :count]
+    # fp32 accumulation of fp16 products, then one fp16 rounding.
+    assert torch.all((got - exp).abs() <= exp.abs() * 2**-10 + 2e-3), float((got - exp).abs().max())
+    if count < rows:
+        assert torch.isnan(out[:, :, count:].float()).all(), "rows past the count must not be written"
+
+
+@pytest.mark.parametrize("rows,count,N,K", [(256, 200, 1024, 1024), (1000, 1000, 768, 3072), (640, 513, 256, 256)])
+def test_gemm_bias_residual_f32(cuda_pkg, rows, count, N, K):
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(rows + N + K)
+    a = torch.randn(rows, K, generator=g).half().to(DEV)
+    w = (torch.randn(N, K, generator=g) / math.sqrt(K)).half().to(DEV)
+    b = torch.randn(N, generator=g).to(DEV)
+    resid = torch.randn(rows + 7, N, generator=g).to(DEV)
+    rmap = torch.randperm(rows + 7, generator=g)[:rows].int().to(DEV)
+    out = k.gemm_bias_residual_f32(a, w, b, resid, resid_map=rmap,
+                                   row_count=torch.tensor([count], dtype=torch.int32, device=DEV))
+    ref = _gemm_ref(a, w, b) + resid[rmap.long()]
+    torch.testing.assert_close(out[:count], ref[:count], rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("rows,N,K", [(512, 4096, 1024), (333, 3072, 768), (128, 1024, 256)])
+def test_gemm_bias_gelu_f16(cuda_pkg, rows, N, K):
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(rows + N)
+    a = torch.randn(rows, K, generator=g).half().to(DEV)
+    w = (torch.randn(N, K, generator=g) / math.sqrt(K)).half().to(DEV)
+    b = torch.randn(N, generator=g).to(DEV)
+    out = k.gemm_bias_gelu_f16(a, w, b).float()
+    ref = torch.nn.functional.gelu(_gemm_ref(a, w, b), approximate="none")
+    assert torch.all((out - ref).abs() <= ref.abs() * 2**-10 + 2e-3), float((out - ref).abs().max())
+
+
+def _attn_ref(q, k, v, q_cu, kv_off, kv_len, scale, causal=False):
+    """q [H, rows, 64] fp16; k/v [G, H, rows, 64]; fp32 math per sample."""
+    H = q.shape[0]
+    out = torch.zeros(q.shape[1], H * 64, dtype=torch.float32, device=q.device)
+    B = q_cu.numel() - 1
+    G = k.shape[0]
+    for b in range(B):
+        q0, q1 = int(q_cu[b]), int(q_cu[b + 1])
+        if q1 == q0:
+            continue
+        ks, vs = [], []
+        for gidx in range(G):
+            o, l = int(kv_off[b, gidx]), int(kv_len[b, gidx])
+            ks.append(k[gidx, :, o : o + l].float())
+            vs.append(v[gidx, :, o : o + l].float())
+        kk = torch.cat(ks, dim=1)
+        vv = torch.cat(vs, dim=1)
+        s = torch.matmul(q[:, q0:q1].float(), kk.transpose(-1, -2)) * scale
+        if causal:
+            qp = torch.arange(q1 - q0, device=q.device)[:, None]
+            kp = torch.arange(kk.shape[1], device=q.device)[None, :]
+            s = s.masked_fill(kp > qp, float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        out[q0:q1] = torch.matmul(p, vv).transpose(0, 1).reshape(q1 - q0, H * 64)
+    return out
+
+
+@pytest.mark.parametrize(
+    "lengths,H",
+    [([1], 1), ([128], 2), ([200, 1, 0, 129], 4), ([1024, 1536, 2048, 700], 16), ([127, 255, 383], 12)],
+)
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_attention_compact(cuda_pkg, lengths, H, causal):
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(sum(lengths) + H)
+    lens = torch.tensor(lengths, dtype=torch.int32)
+    cu = torch.zeros(len(lengths) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    rows = int(cu[-1]) + 64  # slack rows hold garbage (NaN) that must never leak in
+    qkv = torch.randn(3, H, rows, 64, generator=g).half()
+    qkv[:, :, int(cu[-1]):] = float("nan")
+    qkv = qkv.to(DEV)
+    q, kk, vv = qkv[0], qkv[1:2], qkv[2:3]
+    kv_off = cu[:-1].view(-1, 1).contiguous()
+    kv_len = lens.view(-1, 1).contiguous()
+    scale = 64**-0.5
+    out = k.flash_attn_fwd(q, kk, vv, cu.to(DEV), kv_off.to(DEV), kv_len.to(DEV), max(lengths), scale,
+                           causal=causal)
+    ref = _attn_ref(q, kk, vv, cu, kv_off, kv_len, scale, causal)
+    n = int(cu[-1])
+    err = (out[:n].float() - ref[:n]).abs()
+    assert torch.isfinite(out[:n].float()).all()
+    assert float(err.max()) < 4e-3, float(err.max())
+
+
+def test_flash_attention_segments(cuda_pkg):
+    """Two key segments per sample (the context-parallel layout [G][H][rows][64])."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(11)
+    H, G, seg_rows = 4, 2, 512
+    q_rows = 300
+    q = torch.randn(H, q_rows, 64, generator=g).half().to(DEV)
+    kv = torch.randn(G, 2, H, seg_rows, 64, generator=g).half().to(DEV)
+    kk, vv = kv[:, 0], kv[:, 1]
+    q_cu = torch.tensor([0, q_rows], dtype=torch.int32)
+    kv_off = torch.tensor([[0, 0]], dtype=torch.int32)
+    kv_len = torch.tensor([[512, 389]], dtype=torch.int32)
+    out = k.flash_attn_fwd(q, kk, vv, q_cu.to(DEV), kv_off.to(DEV), kv_len.to(DEV), q_rows, 0.125)
+    ref = _attn_ref(q, kk, vv, q_cu, kv_off, kv_len, 0.125)
+    assert float((out.float() - ref).abs().max()) < 4e-3
