@@ -1,0 +1,531 @@
+#!/usr/bin/env python3
+"""Throughput benchmark of the B200 encoder layer (UserOptimizedTransformer.forward).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload dense|short|batch|long]
+
+Metric: layer-forward tokens/s = B*S / step time (padded tokens counted, the
+reference's definition, torch_transformer_benchmark.py:565-567).  A step is
+one forward of one synthetic batch already resident in HBM.  Default workload
+(`dense`): B=8, S=2048, d_model=1024, 16 heads, FFN 4096, one layer,
+non-causal, right-padded mask with lengths ~ U[1024, 2048], LayerNorm
+gamma ~ 1+0.02N(0,1), beta ~ 0.02N(0,1), seeded default-init weights.
+
+Multi-GPU (torchrun, one rank per GPU): batch sharding with no data-path
+collective; each rank runs its own B=8 batch (weak scaling).  The step time is
+the max over ranks of the CUDA-event time of the K timed steps.
+
+Rank 0 prints one JSON line.  `--impl reference` times the reference's CPU
+FP32 path (the oracle restatement of BaselineTransformer) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: (B, S, D, H, F, layers, causal, padding_ratio, ln_perturb, description)
+    "dense": (8, 2048, 1024, 16, 4096, 1, False, 0.5, True,
+              "dense encoder layer B=8 S=2048 d_model=1024 H=16 FFN=4096, L~U[S/2,S]"),
+    "batch": (32, 4096, 1024, 16, 4096, 1, False, 0.75, True,
+              "batch-sharded encoder layer B=32 S=4096 d_model=1024 H=16 FFN=4096, L~U[S/4,S]"),
+    "short": (64, 128, 768, 12, 3072, 1, False, 0.999, False,
+              "short-sequence heavy-padding layer B=64 S=128 d_model=768 H=12 FFN=3072, L~U[1,S]"),
+    "long": (1, 131072, 1024, 16, 4096, 1, False, 0.1, False,
+             "long single sequence B=1 S=131072 d_model=1024 H=16 FFN=4096, L~U[0.9S,S]"),
+}
+
+PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAK_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, backend):
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+
+
+def barrier(world, device=None):
+    if world > 1:
+        import torch.distributed as dist
+
+        if device is not None:
+            dist.barrier(device_ids=[device.index])
+        else:
+            dist.barrier()
+
+
+def max_over_ranks(world, value, device):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL,
+            )
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm = float(r[1])
+                mx = float(r[2])
+            except (ValueError, IndexError):
+                continue
+            sms.append(sm)
+            maxes.append(mx)
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return None
+        loaded = [s for s in sms if s > 0.5 * max(sms)]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------
+# Workload construction
+# ---------------------------------------------------------------------------
+def build_case(workload, rank, device):
+    import oracle
+
+    B, S, D, H, F, L, causal, pad, ln, _ = WORKLOADS[workload]
+    cfg = oracle.TransformerConfig(B, S, D, H, F, L, causal)
+    sd = oracle.make_state_dict(cfg, seed=1234)
+    if ln:
+        sd = oracle.perturb_layernorm(sd, 1234)
+    # Timing inputs use seed + 100000 as the reference harness does
+    # (torch_transformer_benchmark.py:533); each rank draws its own batch.
+    x, mask = oracle.generate_random_case(cfg, seed=1234 + 100000 + 7919 * rank, padding_ratio=pad)
+    return cfg, sd, x, mask
+
+
+def algorithmic_work(cfg, mask):
+    """Valid-token FLOPs of one layer forward and per-kernel units."""
+    lens = mask.sum(1).double()
+    D, F = cfg.d_model, cfg.ffn_dim
+    nv = float(lens.sum())
+    attn = float((4.0 * lens * lens * D).sum())  # QK^T + PV, non-causal
+    gemm = nv * (8.0 * D * D + 4.0 * D * F)
+    return nv, gemm * cfg.num_layers, attn * cfg.num_layers
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    import __graft_entry__
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    init_dist(world, "nccl")
+    pkg = __graft_entry__.load_package()
+    cfg, sd, x_cpu, mask_cpu = build_case(args.workload, rank, device)
+    B, S, D = cfg.batch_size, cfg.seq_len, cfg.d_model
+    model = pkg.UserOptimizedTransformer(pkg.TransformerConfig(*cfg.__dict__.values()))
+    model.load_state_dict(sd, strict=True)
+    model = model.to(device).eval()
+    mask = mask_cpu.to(device)
+    # Inputs larger than L2 between timed steps: x rotates over buffers whose
+    # total exceeds the 126 MB L2 (and every step writes ~1 GB of activations).
+    x_bytes = x_cpu.numel() * 4
+    n_rot = max(2, math.ceil(256e6 / x_bytes))
+    xs = [x_cpu.to(device) for _ in range(n_rot)]
+    stream = torch.cuda.current_stream(device)
+
+    with torch.inference_mode():
+        for i in range(args.warmup):
+            model(xs[i % n_rot], mask)
+        torch.cuda.synchronize(device)
+        pkg._lib.device_status(stream.cuda_stream)
+
+        sampler = ClockSampler(local)
+        sampler.start()
+        time.sleep(0.3)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world, device)
+        torch.cuda.synchronize(device)
+        start.record(stream)
+        for i in range(args.steps):
+            model(xs[i % n_rot], mask)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        clocks = sampler.stop()
+        ms_total = start.elapsed_time(end)
+        pkg._lib.device_status(stream.cuda_stream)
+    ms_total = max_over_ranks(world, ms_total, device)
+    ms_step = ms_total / args.steps
+    tokens_per_step = B * S * world
+    value = tokens_per_step / (ms_step / 1e3)
+
+    e2e = measure_e2e(model, x_cpu, mask_cpu, device, args, world)
+    kernels = kernel_breakdown(pkg, model, cfg, xs[0], mask, device, args)
+    nv, gemm_flops, attn_flops = algorithmic_work(cfg, mask_cpu)
+
+    line = None
+    if rank == 0:
+        peaks, peak_kind = load_peaks()
+        roof = roofline(kernels, peaks, peak_kind)
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(args.workload, budget_s=args.cpu_budget)
+        line = {
+            "metric": "layer-forward tokens/s",
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp16 operands, fp32 accumulate/LayerNorm/residual/output",
+            "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
+            "config": {
+                "workload": WORKLOADS[args.workload][-1],
+                "global_batch": B * world,
+                "seq_len": S,
+                "d_model": D,
+                "heads": cfg.num_heads,
+                "ffn_dim": cfg.ffn_dim,
+                "layers": cfg.num_layers,
+                "parallelism": f"batch-sharded x{world} (no data-path collective)",
+                "valid_tokens_per_gpu": int(nv),
+                "l2": f"inputs larger than L2: x rotates over {n_rot} buffers of {x_bytes / 2**20:.0f} MiB; "
+                      "each step writes ~1 GB of activations",
+            },
+            "tflops_valid": (gemm_flops + attn_flops) * world / (ms_step / 1e3) / 1e12,
+            "e2e": e2e,
+            "gpu_launches": (2 + 7 * cfg.num_layers) * args.steps,
+            "roofline": roof,
+            "kernels": kernels,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+        dist.destroy_process_group()
+    return line
+
+
+def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
+    """Same metric through the public API with host buffers: pinned x -> device,
+    forward, output -> pinned host, every step inside the timed region."""
+    x_host = x_cpu.pin_memory()
+    m_host = mask_cpu.pin_memory()
+    out_host = torch.empty_like(x_cpu).pin_memory()
+    steps = max(3, min(args.steps, 30))
+    stream = torch.cuda.current_stream(device)
+    with torch.inference_mode():
+        for _ in range(2):
+            out_host.copy_(model(x_host.to(device, non_blocking=True), m_host.to(device, non_blocking=True)),
+                           non_blocking=True)
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world, device)
+        torch.cuda.synchronize(device)
+        start.record(stream)
+        for _ in range(steps):
+            xd = x_host.to(device, non_blocking=True)
+            md = m_host.to(device, non_blocking=True)
+            out_host.copy_(model(xd, md), non_blocking=True)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    ms = max_over_ranks(world, start.elapsed_time(end), device) / steps
+    B, S, _ = x_cpu.shape
+    return {
+        "value": B * S * world / (ms / 1e3),
+        "unit": "tokens/s",
+        "ms_per_step": ms,
+        "steps": steps,
+        "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
+        "d2h_bytes_per_step": x_cpu.numel() * 4,
+    }
+
+
+def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
+    """Times each kernel alone through its C-ABI entry point on the workload's
+    buffers (CUDA events on the launching stream, averaged over repeats)."""
+    k = pkg.kernels
+    B, S, D, H, F = cfg.batch_size, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim
+    rows = B * S
+    layer = model.layers[0]
+    att = layer.attention
+    plan = k.token_plan(mask, B, S, device)
+    nv_t, cu, cnt, orig, inv = k.plan_views(plan, B, S)
+    nv = int(nv_t.item())
+    lens = cnt.double().cpu()
+    a16 = torch.empty(rows, D, dtype=torch.float16, device=device)
+    qkv = torch.empty(3, H, rows, 64, dtype=torch.float16, device=device)
+    ctx = torch.empty(rows, D, dtype=torch.float16, device=device)
+    x1 = torch.empty(rows, D, dtype=torch.float32, device=device)
+    h16 = torch.empty(rows, F, dtype=torch.float16, device=device)
+    x2 = torch.empty(rows, D, dtype=torch.float32, device=device)
+    out = torch.empty(rows, D, dtype=torch.float32, device=device)
+    xf = x.view(rows, D)
+    kv_off = cu[:-1].contiguous()
+    ops = {
+        "token_plan": (lambda: k.token_plan(mask, B, S, device), "hbm", rows * (1 + 8)),
+        "ln1_cast_f16": (lambda: k.ln_cast_f16(xf, layer.norm1.weight, layer.norm1.bias, row_map=orig,
+                                               row_count=nv_t, out=a16), "hbm", nv * D * (4 + 2)),
+        "gemm_qkv": (lambda: k.gemm_qkv_headmajor(a16, att._qkv_weight_mixed, att._qkv_bias_mixed, H,
+                                                  row_count=nv_t, out=qkv), "tensor", 2.0 * nv * 3 * D * D),
+        "flash_attn": (lambda: k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, kv_off.view(-1, 1),
+                                                cnt.view(-1, 1), S, 64**-0.5, out=ctx), "tensor",
+                       float((4.0 * lens * lens * D).sum())),
+        "gemm_out_resid": (lambda: k.gemm_bias_residual_f32(ctx, att._out_weight_mixed, att.out_proj.bias, xf,
+                                                            resid_map=orig, row_count=nv_t, out=x1),
+                           "tensor", 2.0 * nv * D * D),
+        "ln2_cast_f16": (lambda: k.ln_cast_f16(x1, layer.norm2.weight, layer.norm2.bias, row_count=nv_t,
+                                               out=a16), "hbm", nv * D * (4 + 2)),
+        "gemm_ffn_in_gelu": (lambda: k.gemm_bias_gelu_f16(a16, layer._ffn_in_weight_mixed, layer.ffn_in.bias,
+                                                          row_count=nv_t, out=h16), "tensor", 2.0 * nv * F * D),
+        "gemm_ffn_out_resid": (lambda: k.gemm_bias_residual_f32(h16, layer._ffn_out_weight_mixed,
+                                                                layer.ffn_out.bias, x1, row_count=nv_t, out=x2),
+                               "tensor", 2.0 * nv * D * F),
+        "ln_final_mask": (lambda: k.ln_final_mask(x2, model.final_norm.weight, model.final_norm.bias,
+                                                  inv_map=inv, rows=rows, out=out), "hbm",
+                          nv * D * 8 + (rows - nv) * D * 4),
+    }
+    stream = torch.cuda.current_stream(device)
+    reps = max(3, min(50, args.steps))
+    res = {}
+    with torch.inference_mode():
+        for name, (fn, bound, work) in ops.items():
+            fn()
+            fn()
+            torch.cuda.synchronize(device)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            for _ in range(reps):
+                fn()
+            e.record(stream)
+            torch.cuda.synchronize(device)
+            ms = s.elapsed_time(e) / reps
+            res[name] = {"ms": ms, "bound": bound, "work": work,
+                         "rate": work / (ms / 1e3) / (1e12 if bound == "tensor" else 1e9),
+                         "unit": "TFLOP/s" if bound == "tensor" else "GB/s"}
+    return res
+
+
+def roofline(kernels, peaks, peak_kind):
+    name, k = max(kernels.items(), key=lambda kv: kv[1]["ms"])
+    if k["bound"] == "tensor":
+        peak = peaks["bf16_tflops"]
+        unit = "TFLOP/s"
+    else:
+        peak = peaks["hbm_gbs"]
+        unit = "GB/s"
+    traffic = load_traffic(name)
+    return {
+        "kernel": name,
+        "bound": "tensor" if k["bound"] == "tensor" else "hbm",
+        "achieved": k["rate"],
+        "peak": peak,
+        "unit": unit,
+        "frac": k["rate"] / peak,
+        "peak_source": f"{peak_kind} ({'bf16_tflops burst, kernel timed alone' if unit == 'TFLOP/s' else 'hbm_gbs'})",
+        "traffic": traffic,
+        "algorithmic_per_launch": k["work"],
+    }
+
+
+def load_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(kernel, {}).get("dram_bytes_per_launch")
+    except (ValueError, AttributeError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm (the oracle restatement of the reference's
+# FP32 BaselineTransformer on the host cores)
+# ---------------------------------------------------------------------------
+def cpu_sample(workload, rows):
+    import oracle
+
+    cfg, sd, x, mask = build_case(workload, 0, torch.device("cpu"))
+    one = oracle.TransformerConfig(rows, *list(cfg.__dict__.values())[1:])
+    xs, ms = x[:rows].contiguous(), mask[:rows].contiguous()
+    if cfg.seq_len > 8192:
+        return lambda: oracle.encoder_forward_blocked(sd, one, xs, ms, query_chunk=1024), one
+    return lambda: oracle.encoder_forward(sd, one, xs, ms), one
+
+
+def cpu_baseline(workload, budget_s=20.0):
+    threads = torch.get_num_threads()
+    B, S = WORKLOADS[workload][0], WORKLOADS[workload][1]
+    rows = 1
+    fn, cfg = cpu_sample(workload, rows)
+    t0 = time.perf_counter()
+    fn()
+    one = time.perf_counter() - t0
+    rows = max(1, min(B, int(budget_s / 3 / max(one, 1e-6))))
+    fn, cfg = cpu_sample(workload, rows)
+    fn()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 1:
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 5:
+            break
+    med = statistics.median(times)
+    return {
+        "value": rows * S / med,
+        "unit": "tokens/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{rows} of {B} sequences of the same batch (S={S}), FP32 oracle, median of {len(times)} runs",
+    }
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    B, S = WORKLOADS[args.workload][0], WORKLOADS[args.workload][1]
+    fn, cfg = cpu_sample(args.workload, 1)
+    for _ in range(max(1, min(args.warmup, 2))):
+        fn()
+    budget = args.cpu_budget * 6
+    times = []
+    t_stop = time.perf_counter() + budget
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_stop:
+            break
+    total = sum(times)
+    value = len(times) * S / total
+    return {
+        "metric": "layer-forward tokens/s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": len(times),
+        "steps_requested": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total / len(times) * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
+        "config": {"workload": WORKLOADS[args.workload][-1], "global_batch": B, "seq_len": S},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"one sequence (S={S}) of the batch per step, FP32 oracle restatement "
+                                   "of BaselineTransformer"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="dense")
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    world, rank, local = dist_env()
+    if world != args.gpus and world > 1:
+        ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+    else:
+        line = run_ours(args, world, rank, local)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
