@@ -1,29 +1,33 @@
 // Masked flash attention forward on tcgen05 (head_dim 64), replacing the SDPA
-// call of v16_1_clean.py:505-514 (and the explicit softmax(QK^T*scale)V of the
-// FP32 reference, torch_transformer_benchmark.py:97-117).
+// call of v16_1_clean.py:505-514 (non-causal, [B,1,1,S] key mask) and :491-504
+// (causal), i.e. softmax(QK^T*scale)V of the FP32 reference,
+// torch_transformer_benchmark.py:97-117, with the score matrix never stored.
 //
 // Queries and keys are compact: the token plan packs the valid tokens of each
 // sample densely, so a sample's keys are the rows [off, off+len) of its key
 // segment(s) and padded keys never enter the loop.  A sample may have several
-// key segments (context parallelism: one per rank, gathered by NCCL); they are
-// walked in order as one key sequence.
+// key segments (context parallelism: one per rank, gathered by NCCL), walked
+// in order as one key sequence.
 //
-// One CTA per (128-query tile, head, sample), 192 threads:
-//   warp 0      TMA: Q once, then K and V tiles of 128 keys into a 3-stage ring
-//   warp 1      TMEM allocation; one lane issues S_j = Q K_j^T (M=128,N=128,
-//               K=16 x4) into one of two TMEM S buffers, and O_j = P_j V_j
-//               (M=128,N=64,K=16 x8) into one of two TMEM O buffers
-//   warps 2-5   softmax: thread = query row = TMEM lane.  Reads S_j, keeps the
-//               running max/sum in fp32 (exp2 domain), writes P_j in fp16 to a
-//               128-byte-swizzled shared tile, and folds O_{j-1} into a
-//               register accumulator while the tensor core works on P_j V_j.
-// The S_{j+1} product is issued before P_j V_j, so the tensor core computes the
-// next scores while the softmax warps work on the current tile.
+// One CTA = two 128-query tiles of one (sample, head); 384 threads:
+//   warp 0        TMA producer: Q tiles once, K/V tiles of 128 keys into a
+//                 4-stage ring.  For the last, partial tile of a segment it
+//                 also zeroes the V rows past the segment end in shared memory,
+//                 so stale or foreign rows cannot reach P V even as 0 * NaN.
+//   warp 1        TMEM allocation and MMA issue (one lane):
+//                   S_t = Q_t K_j^T    (SS, M=128 N=128, 4 x K=16)
+//                   O_t += P_t V_j     (TS: P from TMEM, V from shared, 8 x K=16)
+//   warps 4-7     softmax for query tile 0, warps 8-11 for query tile 1;
+//                 thread = query row = TMEM lane.
+// TMEM (512 columns): tile t uses S [256t, +128), P [256t+128, +64) (fp16
+// pairs), O [256t+192, +64) (fp32).
 //
-// Key rows of the last tile past the segment end are masked to -inf and the
-// matching V rows are zeroed in shared memory before P V, so whatever the
-// buffer holds past the segment (another sample's rows, stale memory) cannot
-// reach the output even as 0 * NaN.
+// Softmax per key tile: load the S row, mask only on partial/causal tiles,
+// tree max; the running max is only raised when the new max exceeds it by
+// more than 8 (log2 units), in which case O (in TMEM) and the row sum are
+// rescaled -- otherwise P = exp2(s*scale*log2e - m) stays <= 2^8, safe in fp16.
+// P goes back to TMEM as fp16 and the tensor core accumulates O += P V; the
+// two query tiles' softmax warpgroups alternate with the tensor core.
 #include "common.cuh"
 #include "internal.h"
 
@@ -32,16 +36,16 @@ namespace tj {
 int make_tmap_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                   const uint64_t* strides_elems, const uint32_t* box);
 
-constexpr int kAttnThreads = 192;
-constexpr int kAttnBM = 128;     // queries per CTA
+constexpr int kAttnThreads = 384;
+constexpr int kAttnBM = 128;     // queries per tile (2 tiles per CTA)
 constexpr int kAttnBN = 128;     // keys per tile
 constexpr int kDH = 64;          // head dim
-constexpr int kKVStages = 3;
+constexpr int kKVStages = 4;
 constexpr uint32_t kQBytes = kAttnBM * kDH * 2;   // 16 KB
 constexpr uint32_t kKVBytes = kAttnBN * kDH * 2;  // 16 KB
-constexpr uint32_t kPBytes = kAttnBM * kAttnBN * 2;  // 32 KB (two 64-key swizzle atoms)
-constexpr size_t kAttnSmem = 1024 + kQBytes + 2 * kKVStages * kKVBytes + 2 * kPBytes + 512;
-constexpr uint32_t kAttnTmemCols = 512;  // S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
+constexpr size_t kAttnSmem = 1024 + 2 * kQBytes + 2 * kKVStages * kKVBytes + 512;
+constexpr uint32_t kAttnTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 256 between rescales
 
 struct AttnKernelParams {
   int H, B, G;
@@ -57,7 +61,7 @@ struct AttnKernelParams {
 };
 
 // Walks the key tiles of one sample in order: segment g, tile i inside it.
-// All three roles walk the same sequence, so tile j means the same keys to each.
+// Every role walks the same sequence, so tile j means the same keys to each.
 struct KvWalk {
   const int32_t* off;
   const int32_t* len;
@@ -70,6 +74,8 @@ struct KvWalk {
     g = 0;
     i = 0;
     pos_base = 0;
+    seg_len = 0;
+    seg_off = 0;
     load_segment();
   }
   __device__ void load_segment() {
@@ -94,50 +100,69 @@ struct KvWalk {
   }
 };
 
-__device__ __forceinline__ int count_kv_tiles(const int32_t* len, int G) {
+// Number of key tiles to visit; with causal masking, tiles whose first key is
+// after the last query of the CTA are skipped.
+__device__ __forceinline__ int count_kv_tiles(const int32_t* off, const int32_t* len, int G,
+                                              bool causal, int max_q_pos) {
+  KvWalk w;
+  w.init(off, len, G);
   int t = 0;
-  for (int g = 0; g < G; ++g) {
-    const int l = len[g];
-    if (l > 0) t += (l + kAttnBN - 1) / kAttnBN;
+  while (w.g < G) {
+    if (causal && w.first_pos() > max_q_pos) break;
+    ++t;
+    w.next();
   }
   return t;
 }
+
+// Register split: the producer/MMA warpgroup gives registers to the two
+// softmax warpgroups.  128*kRegsLow + 256*kRegsHigh must not exceed the
+// registers the CTA is launched with (384 * kLaunchRegs); the launcher checks
+// the kernel's register count before every launch.
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsLow = 56;
+constexpr int kRegsHigh = 224;
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= kAttnThreads * kLaunchRegs, "register split");
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ,
                              const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const AttnKernelParams p) {
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int h = blockIdx.y, b = blockIdx.z;
   const int q_begin = p.q_cu[b];
   const int nq = p.q_cu[b + 1] - q_begin;
-  if (qt * kAttnBM >= nq) return;  // uniform for the CTA
+  const int q_tile0 = blockIdx.x * 2;
+  if (q_tile0 * kAttnBM >= nq) return;  // uniform for the CTA
+  const int ntile = ((q_tile0 + 1) * kAttnBM < nq) ? 2 : 1;
   const int32_t* kv_off = p.kv_off + (int64_t)b * p.kv_len_stride;
   const int32_t* kv_len = p.kv_len + (int64_t)b * p.kv_len_stride;
-  const int T = count_kv_tiles(kv_len, p.G);
+  const int q_pos0 = (p.causal && p.q_pos0) ? p.q_pos0[b] : 0;
+  const int max_q_pos = q_pos0 + min(nq, (q_tile0 + ntile) * kAttnBM) - 1;
+  const int T = count_kv_tiles(kv_off, kv_len, p.G, p.causal != 0, max_q_pos);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kQBytes;
-  uint8_t* sV = sK + kKVStages * kKVBytes;
-  uint8_t* sP = sV + kKVStages * kKVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
-  // q_full, k_full[3], v_full[3], k_empty[3], v_empty[3], s_full[2], s_empty[2],
-  // p_full[2], p_empty[2], o_full[2], o_empty[2], final
+  uint8_t* sQ = smem;                       // 2 x 16 KB
+  uint8_t* sK = sQ + 2 * kQBytes;           // kKVStages x 16 KB
+  uint8_t* sV = sK + kKVStages * kKVBytes;  // kKVStages x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKVStages * kKVBytes);
+  // q_full, k_full[4], v_full[4], k_empty[4], v_empty[4], vfix[4],
+  // s_full[2], s_empty[2], p_full[2], pv_done[2], final
   const uint32_t q_full = smem_u32(bars + 0);
   auto k_full = [&](int s) { return smem_u32(bars + 1 + s); };
-  auto v_full = [&](int s) { return smem_u32(bars + 4 + s); };
-  auto k_empty = [&](int s) { return smem_u32(bars + 7 + s); };
-  auto v_empty = [&](int s) { return smem_u32(bars + 10 + s); };
-  auto s_full = [&](int i) { return smem_u32(bars + 13 + i); };
-  auto s_empty = [&](int i) { return smem_u32(bars + 15 + i); };
-  auto p_full = [&](int i) { return smem_u32(bars + 17 + i); };
-  auto p_empty = [&](int i) { return smem_u32(bars + 19 + i); };
-  auto o_full = [&](int i) { return smem_u32(bars + 21 + i); };
-  auto o_empty = [&](int i) { return smem_u32(bars + 23 + i); };
-  const uint32_t final_bar = smem_u32(bars + 25);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  auto v_full = [&](int s) { return smem_u32(bars + 5 + s); };
+  auto k_empty = [&](int s) { return smem_u32(bars + 9 + s); };
+  auto v_empty = [&](int s) { return smem_u32(bars + 13 + s); };
+  // vfix[s]: the producer has zeroed the V rows past the segment end of the
+  // partial tile in stage s (one phase per partial tile that used the stage).
+  auto vfix = [&](int s) { return smem_u32(bars + 17 + s); };
+  auto s_full = [&](int t) { return smem_u32(bars + 21 + t); };
+  auto s_empty = [&](int t) { return smem_u32(bars + 23 + t); };
+  auto p_full = [&](int t) { return smem_u32(bars + 25 + t); };
+  auto pv_done = [&](int t) { return smem_u32(bars + 27 + t); };
+  const uint32_t final_bar = smem_u32(bars + 29);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_idx();
@@ -150,14 +175,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(v_full(s), 1);
       mbar_init(k_empty(s), 1);
       mbar_init(v_empty(s), 1);
+      mbar_init(vfix(s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(s_full(i), 1);
-      mbar_init(s_empty(i), 4);
-      mbar_init(p_full(i), 4);
-      mbar_init(p_empty(i), 1);
-      mbar_init(o_full(i), 1);
-      mbar_init(o_empty(i), 4);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(s_empty(t), 4);
+      mbar_init(p_full(t), 4);
+      mbar_init(pv_done(t), 1);
     }
     mbar_init(final_bar, 1);
     *abort_flag = device_failed() ? 1 : 0;
@@ -177,248 +201,296 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
       int last_k[kKVStages], last_v[kKVStages];
       for (int s = 0; s < kKVStages; ++s) last_k[s] = last_v[s] = -1;
       bool q_issued = false;
-      if (!*abort_flag) {
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_3d(smem_u32(sQ), &tmQ, q_full, 0, q_begin + qt * kAttnBM, h);
+      if (lane == 0 && !*abort_flag) {
+        mbar_arrive_expect_tx(q_full, ntile * kQBytes);
+        tma_load_3d(smem_u32(sQ), &tmQ, q_full, 0, q_begin + q_tile0 * kAttnBM, h);
+        if (ntile == 2)
+          tma_load_3d(smem_u32(sQ + kQBytes), &tmQ, q_full, 0, q_begin + (q_tile0 + 1) * kAttnBM, h);
         q_issued = true;
       }
       KvWalk w;
       w.init(kv_off, kv_len, p.G);
-      for (int j = 0; j < T && !*abort_flag; ++j, w.next()) {
+      bool ok = true;
+      for (int j = 0; j < T && ok; ++j, w.next()) {
         const int s = j % kKVStages;
         const uint32_t ph = (uint32_t)((j / kKVStages) & 1);
-        if (!mbar_wait(k_empty(s), ph ^ 1, abort_flag, 200)) break;
-        mbar_arrive_expect_tx(k_full(s), kKVBytes);
-        tma_load_4d(smem_u32(sK + s * kKVBytes), &tmK, k_full(s), 0, w.row(), h, w.g);
-        last_k[s] = (int)ph;
-        if (!mbar_wait(v_empty(s), ph ^ 1, abort_flag, 201)) break;
-        mbar_arrive_expect_tx(v_full(s), kKVBytes);
-        tma_load_4d(smem_u32(sV + s * kKVBytes), &tmV, v_full(s), 0, w.row(), h, w.g);
-        last_v[s] = (int)ph;
-      }
-      if (q_issued) {
-        const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
-        }
-      }
-      for (int s = 0; s < kKVStages; ++s) {
-        const unsigned long long t0 = globaltimer_ns();
-        if (last_k[s] >= 0)
-          while (!mbar_try_wait(k_full(s), (uint32_t)last_k[s]) &&
-                 globaltimer_ns() - t0 < kWaitLimitNs) {
+        const int nvalid = w.valid();
+        if (lane == 0) {
+          ok = mbar_wait(k_empty(s), ph ^ 1, abort_flag, 200);
+          if (ok) {
+            mbar_arrive_expect_tx(k_full(s), kKVBytes);
+            tma_load_4d(smem_u32(sK + s * kKVBytes), &tmK, k_full(s), 0, w.row(), h, w.g);
+            last_k[s] = (int)ph;
+            ok = mbar_wait(v_empty(s), ph ^ 1, abort_flag, 201);
           }
-        if (last_v[s] >= 0)
-          while (!mbar_try_wait(v_full(s), (uint32_t)last_v[s]) &&
-                 globaltimer_ns() - t0 < kWaitLimitNs) {
+          if (ok) {
+            mbar_arrive_expect_tx(v_full(s), kKVBytes);
+            tma_load_4d(smem_u32(sV + s * kKVBytes), &tmV, v_full(s), 0, w.row(), h, w.g);
+            last_v[s] = (int)ph;
           }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN, 0, 0);
-      constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, kDH, 0, 1);  // V is MN-major
-      bool issued = false;
-      bool ok = mbar_wait(q_full, 0, abort_flag, 210);
-      if (ok) tc_fence_after();
-      const uint64_t q_desc = sw128_desc(smem_u32(sQ), 16, 1024);
-
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % kKVStages;
-        const uint32_t ph = (uint32_t)((i / kKVStages) & 1);
-        const int buf = i & 1;
-        if (!mbar_wait(v_full(s), ph, abort_flag, 211)) return false;
-        if (!mbar_wait(p_full(buf), (uint32_t)((i >> 1) & 1), abort_flag, 212)) return false;
-        if (i >= 2 && !mbar_wait(o_empty(buf), (uint32_t)(((i - 2) >> 1) & 1), abort_flag, 213))
-          return false;
-        tc_fence_after();
-        const uint32_t d = tmem_base + 256u + (uint32_t)(buf * kDH);
-        const uint32_t p_base = smem_u32(sP + buf * kPBytes);
-        const uint32_t v_base = smem_u32(sV + s * kKVBytes);
-#pragma unroll
-        for (int k = 0; k < kAttnBN / 16; ++k) {
-          // A = P (K-major, two 64-key atoms of 16 KB), B = V (MN-major, 16 key
-          // rows of 128 bytes per K=16 step).
-          const uint64_t a_desc =
-              sw128_desc(p_base + (uint32_t)((k >> 2) * (kAttnBM * 128)) + (uint32_t)((k & 3) * 32),
-                         16, 1024);
-          const uint64_t b_desc = sw128_desc(v_base + (uint32_t)(k * 16 * 128), 1024, 1024);
-          mma_f16_ss(d, a_desc, b_desc, idesc_o, k != 0 ? 1u : 0u);
         }
-        mma_commit(o_full(buf));
-        mma_commit(v_empty(s));
-        mma_commit(p_empty(buf));
-        return true;
-      };
-
-      for (int j = 0; ok && j < T; ++j) {
-        const int s = j % kKVStages;
-        const uint32_t ph = (uint32_t)((j / kKVStages) & 1);
-        const int buf = j & 1;
-        if (!mbar_wait(k_full(s), ph, abort_flag, 214)) break;
-        if (j >= 2 && !mbar_wait(s_empty(buf), (uint32_t)(((j - 2) >> 1) & 1), abort_flag, 215))
-          break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(buf * kAttnBN);
-        const uint64_t k_desc = sw128_desc(smem_u32(sK + s * kKVBytes), 16, 1024);
-#pragma unroll
-        for (int k = 0; k < kDH / 16; ++k)
-          mma_f16_ss(d, q_desc + (uint64_t)(2 * k), k_desc + (uint64_t)(2 * k), idesc_s,
-                     k != 0 ? 1u : 0u);
-        issued = true;
-        mma_commit(s_full(buf));
-        mma_commit(k_empty(s));
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (ok && nvalid < kAttnBN) {
+          // Zero V rows [nvalid, 128) once the tile has landed.
+          ok = mbar_wait(v_full(s), ph, abort_flag, 202);
+          ok = __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
+          if (ok) {
+            for (int r = nvalid + (int)lane; r < kAttnBN; r += 32) {
+              uint4* vrow = reinterpret_cast<uint4*>(sV + s * kKVBytes + r * 128);
+  #pragma unroll
+              for (int c = 0; c < 8; ++c) vrow[c] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(vfix(s));
+          }
         }
       }
-      if (ok && T > 0 && !*abort_flag) issue_pv(T - 1);
-      if (issued) {
-        mma_commit(final_bar);
-        const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try_wait(final_bar, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      if (lane == 0) {
+        // Let every issued load land before the CTA can exit.
+        if (q_issued) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+          }
+        }
+        for (int s = 0; s < kKVStages; ++s) {
+          const unsigned long long t0 = globaltimer_ns();
+          if (last_k[s] >= 0)
+            while (!mbar_try_wait(k_full(s), (uint32_t)last_k[s]) && globaltimer_ns() - t0 < kWaitLimitNs) {
+            }
+          if (last_v[s] >= 0)
+            while (!mbar_try_wait(v_full(s), (uint32_t)last_v[s]) && globaltimer_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN, 0, 0);
+        constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, kDH, 0, 1);  // V is MN-major
+        bool issued = false;
+        bool ok = mbar_wait(q_full, 0, abort_flag, 210);
+        if (ok) tc_fence_after();
+        int nfix[kKVStages] = {0, 0, 0, 0};
+        auto issue_pv = [&](int i, bool boundary) -> bool {
+          const int s = i % kKVStages;
+          const uint32_t ph = (uint32_t)((i / kKVStages) & 1);
+          if (!mbar_wait(v_full(s), ph, abort_flag, 211)) return false;
+          if (boundary) {
+            if (!mbar_wait(vfix(s), (uint32_t)(nfix[s] & 1), abort_flag, 212)) return false;
+            ++nfix[s];
+          }
+          const uint32_t v_base = smem_u32(sV + s * kKVBytes);
+          for (int t = 0; t < ntile; ++t) {
+            if (!mbar_wait(p_full(t), (uint32_t)(i & 1), abort_flag, 213)) return false;
+            tc_fence_after();
+            const uint32_t o_tmem = tmem_base + (uint32_t)(t * 256 + 192);
+            const uint32_t p_tmem = tmem_base + (uint32_t)(t * 256 + 128);
+  #pragma unroll
+            for (int k = 0; k < kAttnBN / 16; ++k) {
+              // B = V (MN-major): K=16 keys = 16 rows of 128 bytes per step.
+              const uint64_t b_desc = sw128_desc(v_base + (uint32_t)(k * 16 * 128), 1024, 1024);
+              mma_f16_ts(o_tmem, p_tmem + (uint32_t)(k * 8), b_desc, idesc_o, (i | k) != 0 ? 1u : 0u);
+            }
+            mma_commit(pv_done(t));
+          }
+          mma_commit(v_empty(s));
+          return true;
+        };
+
+        KvWalk w;
+        w.init(kv_off, kv_len, p.G);
+        bool prev_boundary = false;
+        for (int j = 0; ok && j < T; ++j, w.next()) {
+          const int s = j % kKVStages;
+          const uint32_t ph = (uint32_t)((j / kKVStages) & 1);
+          if (!mbar_wait(k_full(s), ph, abort_flag, 214)) break;
+          const uint64_t k_desc = sw128_desc(smem_u32(sK + s * kKVBytes), 16, 1024);
+          for (int t = 0; t < ntile && ok; ++t) {
+            if (j >= 1 && !mbar_wait(s_empty(t), (uint32_t)((j - 1) & 1), abort_flag, 215)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t q_desc = sw128_desc(smem_u32(sQ + t * kQBytes), 16, 1024);
+            const uint32_t s_tmem = tmem_base + (uint32_t)(t * 256);
+  #pragma unroll
+            for (int k = 0; k < kDH / 16; ++k)
+              mma_f16_ss(s_tmem, q_desc + (uint64_t)(2 * k), k_desc + (uint64_t)(2 * k), idesc_s,
+                         k != 0 ? 1u : 0u);
+            mma_commit(s_full(t));
+            issued = true;
+          }
+          if (!ok) break;
+          mma_commit(k_empty(s));
+          if (j >= 1 && !issue_pv(j - 1, prev_boundary)) {
+            ok = false;
+            break;
+          }
+          prev_boundary = w.valid() < kAttnBN;
+        }
+        if (ok && T > 0 && !*abort_flag) issue_pv(T - 1, prev_boundary);
+        if (issued) {
+          mma_commit(final_bar);
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(final_bar, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+          }
         }
       }
     }
   } else {
-    // Softmax warps.
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    // ------------------------------------------------------------ softmax
+    const int t = (warp - 4) >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;
-    const int row = quarter * 32 + (int)lane;  // query row in the tile = TMEM lane
-    const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    const float sl2 = p.scale_log2;
-    const int q_local = qt * kAttnBM + row;
-    const int q_pos = (p.causal && p.q_pos0 ? p.q_pos0[b] : 0) + q_local;
-    float m_run = -INFINITY;  // running max of s*sl2
-    float l_run = 0.f;
-    float alpha_prev = 0.f;
-    float acc[kDH];
-#pragma unroll
-    for (int d = 0; d < kDH; ++d) acc[d] = 0.f;
-    bool ok = true;
+    const int row = quarter * 32 + (int)lane;
+    if (t < ntile) {
+      const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * 256);
+      const uint32_t s_tmem = t_lane, p_tmem = t_lane + 128u, o_tmem = t_lane + 192u;
+      const float sl2 = p.scale_log2;
+      const int q_local = (q_tile0 + t) * kAttnBM + row;
+      const int q_pos = q_pos0 + q_local;
+      float m_run = -INFINITY;  // running max (log2 units, stale by at most 8)
+      float l_run = 0.f;
+      bool ok = true;
 
-    auto fold_o = [&](int i) -> bool {
-      const int buf = i & 1;
-      if (!mbar_wait(o_full(buf), (uint32_t)((i >> 1) & 1), abort_flag, 220)) return false;
-      tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld32(t_lane + 256u + (uint32_t)(buf * kDH), r0);
-      tmem_ld32(t_lane + 256u + (uint32_t)(buf * kDH) + 32u, r1);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_empty(buf));
-#pragma unroll
-      for (int d = 0; d < 32; ++d) acc[d] = fmaf(acc[d], alpha_prev, __uint_as_float(r0[d]));
-#pragma unroll
-      for (int d = 0; d < 32; ++d)
-        acc[32 + d] = fmaf(acc[32 + d], alpha_prev, __uint_as_float(r1[d]));
-      return true;
-    };
-
-    KvWalk w;
-    w.init(kv_off, kv_len, p.G);
-    for (int j = 0; j < T; ++j, w.next()) {
-      const int buf = j & 1;
-      const int s = j % kKVStages;
-      if (!mbar_wait(s_full(buf), (uint32_t)((j >> 1) & 1), abort_flag, 221)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sr[kAttnBN];
-      tmem_ld32(t_lane + (uint32_t)(buf * kAttnBN) + 0u, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
-      tmem_ld32(t_lane + (uint32_t)(buf * kAttnBN) + 32u, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-      tmem_ld32(t_lane + (uint32_t)(buf * kAttnBN) + 64u, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-      tmem_ld32(t_lane + (uint32_t)(buf * kAttnBN) + 96u, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(buf));
-
-      const int nvalid = w.valid();
-      const int kp0 = w.first_pos();
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kAttnBN; ++c) {
-        float x = __uint_as_float(sr[c]);
-        if (c >= nvalid || (p.causal && kp0 + c > q_pos)) x = -INFINITY;
-        sr[c] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
-      }
-      const float m_new = fmaxf(m_run, mx * sl2);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = exp2_approx(m_run - m_use);
-      m_run = m_new;
-
-      // P_j -> shared (wait until P_{j-2} V_{j-2} has finished reading it).
-      if (j >= 2 && !mbar_wait(p_empty(buf), (uint32_t)(((j - 2) >> 1) & 1), abort_flag, 222)) {
-        ok = false;
-        break;
-      }
-      float rowsum = 0.f;
-      uint8_t* prow = sP + buf * kPBytes + row * 128;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float e[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          e[u] = exp2_approx(fmaf(__uint_as_float(sr[8 * c + u]), sl2, -m_use));
-          rowsum += e[u];
-        }
-        const uint4 v4 = make_uint4(pack_half2(e[0], e[1]), pack_half2(e[2], e[3]),
-                                    pack_half2(e[4], e[5]), pack_half2(e[6], e[7]));
-        const int atom = c >> 3, cc = c & 7;
-        *reinterpret_cast<uint4*>(prow + atom * (kAttnBM * 128) + ((cc ^ (row & 7)) << 4)) = v4;
-      }
-      l_run = l_run * alpha + rowsum;
-      if (nvalid < kAttnBN) {
-        // Zero the V rows past the segment end (thread `row` owns key row `row`).
-        if (!mbar_wait(v_full(s), (uint32_t)((j / kKVStages) & 1), abort_flag, 223)) {
+      KvWalk w;
+      w.init(kv_off, kv_len, p.G);
+      for (int j = 0; j < T; ++j, w.next()) {
+        if (!mbar_wait(s_full(t), (uint32_t)(j & 1), abort_flag, 220)) {
           ok = false;
           break;
         }
-        if (row >= nvalid) {
-          uint4* vrow = reinterpret_cast<uint4*>(sV + s * kKVBytes + row * 128);
+        tc_fence_after();
+        uint32_t sr[kAttnBN];
+        tmem_ld32(s_tmem + 0u, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
+        tmem_ld32(s_tmem + 32u, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+        tmem_ld32(s_tmem + 64u, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
+        tmem_ld32(s_tmem + 96u, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty(t));
+
+        // Keys c >= lim are masked: the segment end, and for causal masking
+        // the keys after this query.
+        int lim = w.valid();
+        if (p.causal) lim = min(lim, q_pos - w.first_pos() + 1);
+        if (lim < kAttnBN) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) vrow[c] = make_uint4(0u, 0u, 0u, 0u);
+          for (int c = 0; c < kAttnBN; ++c)
+            if (c >= lim) sr[c] = __float_as_uint(-INFINITY);
+        }
+        float pm[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) pm[u] = __uint_as_float(sr[u]);
+#pragma unroll
+        for (int c = 8; c < kAttnBN; c += 8)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], __uint_as_float(sr[c + u]));
+        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        const float m_cand = fmaxf(m_run, mx * sl2);
+
+        // P_{j-1} V_{j-1} must be done: it reads the P buffer and writes O.
+        if (j >= 1) {
+          if (!mbar_wait(pv_done(t), (uint32_t)((j - 1) & 1), abort_flag, 221)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        const bool need = __any_sync(0xffffffffu, m_cand > m_run + kRescaleThreshold);
+        if (need) {
+          const float alpha = (m_cand == -INFINITY) ? 1.f : exp2_approx(m_run - m_cand);
+          if (j >= 1) {
+            uint32_t o[32];
+            tmem_ld32(o_tmem, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+            tmem_st32(o_tmem, o);
+            tmem_ld32(o_tmem + 32u, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+            tmem_st32(o_tmem + 32u, o);
+          }
+          l_run *= alpha;
+          if (m_cand != -INFINITY) m_run = m_cand;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        const float2 sl2v = make_float2(sl2, sl2);
+        const float2 negm = make_float2(-m_use, -m_use);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int e = half * 64 + 2 * c;
+            float2 x = ffma2(make_float2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), sl2v, negm);
+            x.x = exp2_approx(x.x);
+            x.y = exp2_approx(x.y);
+            acc[c & 3] = fadd2(acc[c & 3], x);
+            pk[c] = pack_half2(x.x, x.y);
+          }
+          tmem_st32(p_tmem + (uint32_t)(half * 32), pk);
+        }
+        tmem_st_wait();
+        const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
+        const float2 a = fadd2(a01, a23);
+        l_run += a.x + a.y;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full(t));
+      }
+      if (ok && T > 0) {
+        ok = mbar_wait(pv_done(t), (uint32_t)((T - 1) & 1), abort_flag, 222);
+        if (ok) tc_fence_after();
+      }
+      ok = __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
+      if (ok) {
+        const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
+        uint32_t o0[32], o1[32];
+        if (T > 0) {
+          tmem_ld32(o_tmem, o0);
+          tmem_ld32(o_tmem + 32u, o1);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int d = 0; d < 32; ++d) o0[d] = o1[d] = 0u;
+        }
+        if (q_local < nq) {
+          __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * kDH;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 v;
+            v.x = pack_half2(__uint_as_float(o0[8 * c + 0]) * inv_l, __uint_as_float(o0[8 * c + 1]) * inv_l);
+            v.y = pack_half2(__uint_as_float(o0[8 * c + 2]) * inv_l, __uint_as_float(o0[8 * c + 3]) * inv_l);
+            v.z = pack_half2(__uint_as_float(o0[8 * c + 4]) * inv_l, __uint_as_float(o0[8 * c + 5]) * inv_l);
+            v.w = pack_half2(__uint_as_float(o0[8 * c + 6]) * inv_l, __uint_as_float(o0[8 * c + 7]) * inv_l);
+            reinterpret_cast<uint4*>(dst)[c] = v;
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 v;
+            v.x = pack_half2(__uint_as_float(o1[8 * c + 0]) * inv_l, __uint_as_float(o1[8 * c + 1]) * inv_l);
+            v.y = pack_half2(__uint_as_float(o1[8 * c + 2]) * inv_l, __uint_as_float(o1[8 * c + 3]) * inv_l);
+            v.z = pack_half2(__uint_as_float(o1[8 * c + 4]) * inv_l, __uint_as_float(o1[8 * c + 5]) * inv_l);
+            v.w = pack_half2(__uint_as_float(o1[8 * c + 6]) * inv_l, __uint_as_float(o1[8 * c + 7]) * inv_l);
+            reinterpret_cast<uint4*>(dst)[4 + c] = v;
+          }
         }
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(buf));
-
-      if (j >= 1 && !fold_o(j - 1)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && T > 0 && fold_o(T - 1)) {
-      // done
-    } else {
-      ok = false;
-    }
-    if (ok && q_local < nq) {
-      const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-      __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * kDH;
-#pragma unroll
-      for (int c = 0; c < kDH / 8; ++c) {
-        uint4 o;
-        o.x = pack_half2(acc[8 * c + 0] * inv_l, acc[8 * c + 1] * inv_l);
-        o.y = pack_half2(acc[8 * c + 2] * inv_l, acc[8 * c + 3] * inv_l);
-        o.z = pack_half2(acc[8 * c + 4] * inv_l, acc[8 * c + 5] * inv_l);
-        o.w = pack_half2(acc[8 * c + 6] * inv_l, acc[8 * c + 7] * inv_l);
-        reinterpret_cast<uint4*>(dst)[c] = o;
-      }
-    } else if (T == 0 && q_local < nq) {
-      __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * kDH;
-#pragma unroll
-      for (int c = 0; c < kDH / 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
     }
   }
 
@@ -465,6 +537,15 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   }
   static bool attr_set = false;
   if (!attr_set) {
+    cudaFuncAttributes fa;
+    cudaError_t e0 = cudaFuncGetAttributes(&fa, attention_tcgen05_kernel);
+    if (e0 != cudaSuccess)
+      return set_error(TJ_ERR_CUDA, "attention attributes: %s", cudaGetErrorString(e0));
+    if (fa.numRegs != kLaunchRegs)
+      return set_error(TJ_ERR_UNSUPPORTED,
+                       "attention kernel built with %d registers per thread, the register split "
+                       "assumes %d; refusing to launch",
+                       fa.numRegs, kLaunchRegs);
     cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem);
     if (e != cudaSuccess)
@@ -484,7 +565,7 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   kp.q_pos0 = a.q_pos0;
   kp.ctx = static_cast<__half*>(a.ctx);
   kp.ld_ctx = a.H * kDH;
-  dim3 grid((a.max_q_per_sample + kAttnBM - 1) / kAttnBM, a.H, a.B);
+  dim3 grid((a.max_q_per_sample + 2 * kAttnBM - 1) / (2 * kAttnBM), a.H, a.B);
   if (grid.y > 65535 || grid.z > 65535)
     return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d or B=%d above 65535", a.H, a.B);
   attention_tcgen05_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tq, tk, tv, kp);

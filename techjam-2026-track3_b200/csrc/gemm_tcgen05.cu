@@ -10,13 +10,15 @@
 //   kEpiGeluF16       FFN-in (v16_1_clean.py:221-301, the Triton fused op):
 //                     +bias, exact erf-GELU on the fp32 accumulator, fp16.
 //
-// Structure (one CTA per SM, 192 threads):
+// Structure (one CTA per SM, 320 threads):
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
 //               shared-memory stages, completion on mbarriers.
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128, N=BN,
 //               K=16 per instruction) into one of two TMEM accumulators.
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
-//               lanes 32*(w%4)..+31 = tile rows), fused math, global stores.
+//   warps 2-9   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)..+31 = tile rows; warps 2-5 take the first
+//               half of the tile's columns, warps 6-9 the second), fused math,
+//               global stores.
 // Two accumulators let the epilogue of tile i overlap the main loop of tile
 // i+1.  Tiles are walked n-fastest so CTAs running at the same time share the
 // A tile through L2.  The number of rows comes from device memory (the token
@@ -28,7 +30,8 @@
 
 namespace tj {
 
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kEpiWarps = 8;
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
@@ -100,7 +103,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);
+      mbar_init(tempty_bar(a), kEpiWarps);
     }
     mbar_init(final_bar, 1);
     *abort_flag = device_failed() ? 1 : 0;
@@ -197,8 +200,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    // Epilogue warps 2..9: TMEM lane quarter = warp % 4, column half by warp.
     const int quarter = warp & 3;
+    const int col_half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + (int)lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -214,11 +218,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (EPI == kEpiResidualF32 && row_ok)
         resid_row = p.resid_map ? (int64_t)p.resid_map[row] : (int64_t)row;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int cc = 0; cc < BN / 64; ++cc) {
+        const int c = col_half * (BN / 64) + cc;
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
         const int nc = n0 + c * 32;
+        // Residual loads are issued before the TMEM wait so both latencies overlap.
+        float4 res[8];
+        if (EPI == kEpiResidualF32) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) res[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (row_ok) {
+            const float4* rs = reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + nc);
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              if (nc + 4 * g < p.N) res[g] = __ldg(rs + g);
+          }
+        }
+        tmem_ld_wait();
         if (!row_ok || nc >= p.N) continue;
         float v[32];
 #pragma unroll
@@ -254,9 +271,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             o.w = pack_half2(gelu_erf(w[6]), gelu_erf(w[7]));
             *reinterpret_cast<uint4*>(dst) = o;
           } else {
-            const float4* rs =
-                reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + n);
-            const float4 r0 = __ldg(rs), r1 = __ldg(rs + 1);
+            const float4 r0 = res[2 * g], r1 = res[2 * g + 1];
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
                                                     (int64_t)row * p.ld_out + n);
             dst[0] = make_float4(w[0] + r0.x, w[1] + r0.y, w[2] + r0.z, w[3] + r0.w);
