@@ -185,6 +185,32 @@ TJ_API int tj_encoder_forward(const tj_encoder_desc* desc, const tj_layer_weight
                        const uint8_t* mask, float* out, void* workspace, int64_t workspace_bytes,
                        void* stream);
 
+/* ---- encoder without a caller workspace --------------------------------- */
+
+/* Size of the library's static device workspace used by
+ * tj_encoder_forward_noalloc (64 MiB, held on every GPU that loads the
+ * library until the process exits). */
+#define TJ_NOALLOC_WORKSPACE_BYTES (64ull << 20)
+
+/* Same computation and arguments as tj_encoder_forward, minus the workspace:
+ * scratch space comes from a fixed library-owned device array, so this call
+ * allocates no device memory.  No counterpart in the reference; it exists for
+ * callers that cannot allocate device memory where they run the encoder (a
+ * host binding the library through a thin FFI without a device allocator,
+ * serving code whose device memory is planned up front, or code that must
+ * not let cudaMalloc/cudaFree synchronise the device).
+ *   - Shapes whose tj_encoder_workspace_bytes() exceeds
+ *     TJ_NOALLOC_WORKSPACE_BYTES are rejected with TJ_ERR_WORKSPACE.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (other
+ *     streams or threads) race.  Nothing in it needs to start at zero. */
+TJ_API int tj_encoder_forward_noalloc(const tj_encoder_desc* desc, const tj_layer_weights* layers,
+                                      const float* final_gamma, const float* final_beta,
+                                      const float* x, const uint8_t* mask, float* out,
+                                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -96,6 +96,10 @@ SIGNATURES = {
             c_vp, c_vp, c_i64, c_vp,
         ],
     ),
+    "tj_encoder_forward_noalloc": (
+        c_int,
+        [ctypes.POINTER(EncoderDesc), ctypes.POINTER(LayerWeights), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    ),
 }
 
 _lib = None

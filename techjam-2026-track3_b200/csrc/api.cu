@@ -392,3 +392,7 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
 }
 
 }  // extern "C"
+
+// Workspace-free variant of tj_encoder_forward (its own file: static device
+// workspace and the per-device address lookup).
+#include "noalloc.cu"
