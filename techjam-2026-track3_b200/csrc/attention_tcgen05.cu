@@ -46,6 +46,12 @@ constexpr uint32_t kKVBytes = kAttnBN * kDH * 2;  // 16 KB
 constexpr size_t kAttnSmem = 1024 + 2 * kQBytes + 2 * kKVStages * kKVBytes + 512;
 constexpr uint32_t kAttnTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 256 between rescales
+// Of every 8 exponential pairs, this many run as a polynomial on the FMA pipe
+// and the rest on the MUFU unit (which alone would be the softmax bottleneck).
+#ifndef TJ_ATTN_POLY_PAIRS_PER_8
+#define TJ_ATTN_POLY_PAIRS_PER_8 2
+#endif
+constexpr int kPolyPairsPer8 = TJ_ATTN_POLY_PAIRS_PER_8;
 
 struct AttnKernelParams {
   int H, B, G;
@@ -279,64 +285,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         bool ok = mbar_wait(q_full, 0, abort_flag, 210);
         if (ok) tc_fence_after();
         int nfix[kKVStages] = {0, 0, 0, 0};
-        auto issue_pv = [&](int i, bool boundary) -> bool {
+        // S_t(j) = Q_t K_j^T into the tile's S columns.
+        auto issue_s = [&](int t, int j, uint64_t k_desc) -> bool {
+          if (j >= 1 && !mbar_wait(s_empty(t), (uint32_t)((j - 1) & 1), abort_flag, 215)) return false;
+          tc_fence_after();
+          const uint64_t q_desc = sw128_desc(smem_u32(sQ + t * kQBytes), 16, 1024);
+          const uint32_t s_tmem = tmem_base + (uint32_t)(t * 256);
+#pragma unroll
+          for (int k = 0; k < kDH / 16; ++k)
+            mma_f16_ss(s_tmem, q_desc + (uint64_t)(2 * k), k_desc + (uint64_t)(2 * k), idesc_s,
+                       k != 0 ? 1u : 0u);
+          mma_commit(s_full(t));
+          issued = true;
+          return true;
+        };
+        // O_t += P_t(i) V_i.  The first user of V_i waits for the tile (and, for
+        // a partial tile, for the zeroed rows); the last user releases the stage.
+        auto issue_pv = [&](int t, int i, bool boundary) -> bool {
           const int s = i % kKVStages;
-          const uint32_t ph = (uint32_t)((i / kKVStages) & 1);
-          if (!mbar_wait(v_full(s), ph, abort_flag, 211)) return false;
-          if (boundary) {
-            if (!mbar_wait(vfix(s), (uint32_t)(nfix[s] & 1), abort_flag, 212)) return false;
-            ++nfix[s];
-          }
-          const uint32_t v_base = smem_u32(sV + s * kKVBytes);
-          for (int t = 0; t < ntile; ++t) {
-            if (!mbar_wait(p_full(t), (uint32_t)(i & 1), abort_flag, 213)) return false;
-            tc_fence_after();
-            const uint32_t o_tmem = tmem_base + (uint32_t)(t * 256 + 192);
-            const uint32_t p_tmem = tmem_base + (uint32_t)(t * 256 + 128);
-  #pragma unroll
-            for (int k = 0; k < kAttnBN / 16; ++k) {
-              // B = V (MN-major): K=16 keys = 16 rows of 128 bytes per step.
-              const uint64_t b_desc = sw128_desc(v_base + (uint32_t)(k * 16 * 128), 1024, 1024);
-              mma_f16_ts(o_tmem, p_tmem + (uint32_t)(k * 8), b_desc, idesc_o, (i | k) != 0 ? 1u : 0u);
+          if (t == 0) {
+            if (!mbar_wait(v_full(s), (uint32_t)((i / kKVStages) & 1), abort_flag, 211)) return false;
+            if (boundary) {
+              if (!mbar_wait(vfix(s), (uint32_t)(nfix[s] & 1), abort_flag, 212)) return false;
+              ++nfix[s];
             }
-            mma_commit(pv_done(t));
           }
-          mma_commit(v_empty(s));
+          if (!mbar_wait(p_full(t), (uint32_t)(i & 1), abort_flag, 213)) return false;
+          tc_fence_after();
+          const uint32_t v_base = smem_u32(sV + s * kKVBytes);
+          const uint32_t o_tmem = tmem_base + (uint32_t)(t * 256 + 192);
+          const uint32_t p_tmem = tmem_base + (uint32_t)(t * 256 + 128);
+#pragma unroll
+          for (int k = 0; k < kAttnBN / 16; ++k) {
+            // B = V (MN-major): K=16 keys = 16 rows of 128 bytes per step.
+            const uint64_t b_desc = sw128_desc(v_base + (uint32_t)(k * 16 * 128), 1024, 1024);
+            mma_f16_ts(o_tmem, p_tmem + (uint32_t)(k * 8), b_desc, idesc_o, (i | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(pv_done(t));
+          if (t == ntile - 1) mma_commit(v_empty(s));
           return true;
         };
 
+        // S is issued one key tile ahead: S0(j+1), S1(j+1), then PV0(j),
+        // PV1(j).  A softmax warpgroup releases S(j) as soon as it has the row
+        // in registers, so S(j+1) is computed while it still works on tile j
+        // and its next step can start the moment P(j) is stored.
+        auto issue_s_pair = [&](int j) -> bool {
+          const int s = j % kKVStages;
+          if (!mbar_wait(k_full(s), (uint32_t)((j / kKVStages) & 1), abort_flag, 214)) return false;
+          const uint64_t k_desc = sw128_desc(smem_u32(sK + s * kKVBytes), 16, 1024);
+          for (int t = 0; t < ntile; ++t)
+            if (!issue_s(t, j, k_desc)) return false;
+          mma_commit(k_empty(s));
+          return true;
+        };
         KvWalk w;
         w.init(kv_off, kv_len, p.G);
-        bool prev_boundary = false;
+        if (ok && T > 0) ok = issue_s_pair(0);
         for (int j = 0; ok && j < T; ++j, w.next()) {
-          const int s = j % kKVStages;
-          const uint32_t ph = (uint32_t)((j / kKVStages) & 1);
-          if (!mbar_wait(k_full(s), ph, abort_flag, 214)) break;
-          const uint64_t k_desc = sw128_desc(smem_u32(sK + s * kKVBytes), 16, 1024);
-          for (int t = 0; t < ntile && ok; ++t) {
-            if (j >= 1 && !mbar_wait(s_empty(t), (uint32_t)((j - 1) & 1), abort_flag, 215)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint64_t q_desc = sw128_desc(smem_u32(sQ + t * kQBytes), 16, 1024);
-            const uint32_t s_tmem = tmem_base + (uint32_t)(t * 256);
-  #pragma unroll
-            for (int k = 0; k < kDH / 16; ++k)
-              mma_f16_ss(s_tmem, q_desc + (uint64_t)(2 * k), k_desc + (uint64_t)(2 * k), idesc_s,
-                         k != 0 ? 1u : 0u);
-            mma_commit(s_full(t));
-            issued = true;
-          }
-          if (!ok) break;
-          mma_commit(k_empty(s));
-          if (j >= 1 && !issue_pv(j - 1, prev_boundary)) {
-            ok = false;
-            break;
-          }
-          prev_boundary = w.valid() < kAttnBN;
+          if (j + 1 < T) ok = issue_s_pair(j + 1);
+          const bool boundary = w.valid() < kAttnBN;
+          for (int t = 0; ok && t < ntile; ++t) ok = issue_pv(t, j, boundary);
         }
-        if (ok && T > 0 && !*abort_flag) issue_pv(T - 1, prev_boundary);
         if (issued) {
           mma_commit(final_bar);
           const unsigned long long t0 = globaltimer_ns();
@@ -392,9 +402,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int u = 0; u < 8; ++u) pm[u] = __uint_as_float(sr[u]);
 #pragma unroll
-        for (int c = 8; c < kAttnBN; c += 8)
+        for (int c = 8; c < kAttnBN - 8; c += 16)
 #pragma unroll
-          for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], __uint_as_float(sr[c + u]));
+          for (int u = 0; u < 8; ++u)
+            pm[u] = fmax3(pm[u], __uint_as_float(sr[c + u]), __uint_as_float(sr[c + 8 + u]));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], __uint_as_float(sr[kAttnBN - 8 + u]));
         const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                                fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
         const float m_cand = fmaxf(m_run, mx * sl2);
@@ -438,8 +451,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int c = 0; c < 32; ++c) {
             const int e = half * 64 + 2 * c;
             float2 x = ffma2(make_float2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), sl2v, negm);
-            x.x = exp2_approx(x.x);
-            x.y = exp2_approx(x.y);
+            if ((c & 7) < kPolyPairsPer8) {
+              x = exp2_poly2(x);  // FMA pipe
+            } else {
+              x.x = exp2_approx(x.x);  // MUFU
+              x.y = exp2_approx(x.y);
+            }
             acc[c & 3] = fadd2(acc[c & 3], x);
             pk[c] = pack_half2(x.x, x.y);
           }

@@ -316,6 +316,38 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int a_mn, int
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// 2^x for a pair of floats on the FMA pipe (no MUFU): x = j + r with
+// j = round(x) and r in [-1/2, 1/2]; 2^r from a degree-4 polynomial fitted for
+// this kernel (iteratively reweighted least squares on relative error over
+// [-1/2, 1/2]; max relative error 2.7e-6 evaluated in fp32), then j added to
+// the exponent field.  Inputs below -126 are clamped (the result is then
+// ~1e-38, which the caller rounds to fp16 zero).  Used for part of the
+// softmax exponentials so the MUFU unit and the FMA pipe share the load.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 j = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 r = fadd2(x, make_float2(-j.x, -j.y));
+  float2 p = make_float2(0.009569931775331497f, 0.009569931775331497f);
+  p = ffma2(p, r, make_float2(0.0559174083173275f, 0.0559174083173275f));
+  p = ffma2(p, r, make_float2(0.240247443318367f, 0.240247443318367f));
+  p = ffma2(p, r, make_float2(0.6931218504905701f, 0.6931218504905701f));
+  p = ffma2(p, r, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  const int jx = __float_as_int(t.x) - 0x4B400000;
+  const int jy = __float_as_int(t.y) - 0x4B400000;
+  return make_float2(__int_as_float(__float_as_int(p.x) + (jx << 23)),
+                     __int_as_float(__float_as_int(p.y) + (jy << 23)));
+}
+
+// max(a, b, c) in one instruction (three-input max of sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float exp2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

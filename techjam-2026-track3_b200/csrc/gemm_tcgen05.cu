@@ -10,15 +10,14 @@
 //   kEpiGeluF16       FFN-in (v16_1_clean.py:221-301, the Triton fused op):
 //                     +bias, exact erf-GELU on the fp32 accumulator, fp16.
 //
-// Structure (one CTA per SM, 320 threads):
+// Structure (one CTA per SM, 64 + 32 * epilogue-warps threads):
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
 //               shared-memory stages, completion on mbarriers.
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma (M=128, N=BN,
 //               K=16 per instruction) into one of two TMEM accumulators.
-//   warps 2-9   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
-//               lanes 32*(w%4)..+31 = tile rows; warps 2-5 take the first
-//               half of the tile's columns, warps 6-9 the second), fused math,
-//               global stores.
+//   warps 2..    epilogue (8 or 16 warps): tcgen05.ld of the accumulator (warp
+//               w reads TMEM lanes 32*(w%4)..+31 = tile rows; the warps of a
+//               lane quarter split the tile's columns), fused math, stores.
 // Two accumulators let the epilogue of tile i overlap the main loop of tile
 // i+1.  Tiles are walked n-fastest so CTAs running at the same time share the
 // A tile through L2.  The number of rows comes from device memory (the token
@@ -30,8 +29,11 @@
 
 namespace tj {
 
-constexpr int kGemmThreads = 320;
-constexpr int kEpiWarps = 8;
+// Epilogue warps per CTA: 8 for the residual epilogue (each thread keeps the
+// prefetched residual of its row in registers), 16 for the fp16 epilogues
+// (GELU is ALU-heavy; more warps hide its latency).
+__host__ __device__ constexpr int epi_warps_for(int epi) { return epi == 1 ? 8 : 16; }
+__host__ __device__ constexpr int gemm_threads_for(int epi) { return 64 + 32 * epi_warps_for(epi); }
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
@@ -72,11 +74,12 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(gemm_threads_for(EPI), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmKernelParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
+  constexpr int kEpiWarps = epi_warps_for(EPI);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
@@ -200,55 +203,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..9: TMEM lane quarter = warp % 4, column half by warp.
+    // Epilogue warps: TMEM lane quarter = warp % 4; the kEpiWarps/4 warps of a
+    // quarter split the tile's columns into slices of kChunks x 32.
+    constexpr int kSlices = kEpiWarps / 4;
+    constexpr int kChunks = BN / 32 / kSlices;
     const int quarter = warp & 3;
-    const int col_half = (warp - 2) >> 2;
+    const int slice = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + (int)lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
       const int m0 = (t / n_tiles) * kBM;
       const int n0 = (t % n_tiles) * BN;
-      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, 130 + EPI)) break;
-      tc_fence_after();
       const int row = m0 + row_in_tile;
       const bool row_ok = row < rows;
+      // Residual rows are fetched before waiting for the accumulator, so their
+      // DRAM latency hides behind the tile's main loop.
+      float4 res[EPI == kEpiResidualF32 ? kChunks : 1][8];
+      if (EPI == kEpiResidualF32) {
+        const int64_t resid_row = row_ok ? (p.resid_map ? (int64_t)p.resid_map[row] : (int64_t)row) : 0;
+#pragma unroll
+        for (int cc = 0; cc < kChunks; ++cc) {
+          const int nc = n0 + (slice * kChunks + cc) * 32;
+          const float4* rs = reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + nc);
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            res[cc][g] = (row_ok && nc + 4 * g < p.N) ? __ldg(rs + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, 130 + EPI)) break;
+      tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      int64_t resid_row = 0;
-      if (EPI == kEpiResidualF32 && row_ok)
-        resid_row = p.resid_map ? (int64_t)p.resid_map[row] : (int64_t)row;
-#pragma unroll 1
-      for (int cc = 0; cc < BN / 64; ++cc) {
-        const int c = col_half * (BN / 64) + cc;
+#pragma unroll
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int c = slice * kChunks + cc;
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
-        const int nc = n0 + c * 32;
-        // Residual loads are issued before the TMEM wait so both latencies overlap.
-        float4 res[8];
-        if (EPI == kEpiResidualF32) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g) res[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (row_ok) {
-            const float4* rs = reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + nc);
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              if (nc + 4 * g < p.N) res[g] = __ldg(rs + g);
-          }
-        }
         tmem_ld_wait();
+        const int nc = n0 + c * 32;
         if (!row_ok || nc >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const int n = nc + 8 * g;
           if (n >= p.N) break;
           const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
           const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + n) + 1);
-          float w[8] = {v[8 * g + 0] + b0.x, v[8 * g + 1] + b0.y, v[8 * g + 2] + b0.z,
-                        v[8 * g + 3] + b0.w, v[8 * g + 4] + b1.x, v[8 * g + 5] + b1.y,
-                        v[8 * g + 6] + b1.z, v[8 * g + 7] + b1.w};
+          float w[8] = {__uint_as_float(r[8 * g + 0]) + b0.x, __uint_as_float(r[8 * g + 1]) + b0.y,
+                        __uint_as_float(r[8 * g + 2]) + b0.z, __uint_as_float(r[8 * g + 3]) + b0.w,
+                        __uint_as_float(r[8 * g + 4]) + b1.x, __uint_as_float(r[8 * g + 5]) + b1.y,
+                        __uint_as_float(r[8 * g + 6]) + b1.z, __uint_as_float(r[8 * g + 7]) + b1.w};
           if (EPI == kEpiQkvHeadMajor) {
             const int which = n / p.d_model;
             const int rem = n - which * p.d_model;
@@ -271,7 +274,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             o.w = pack_half2(gelu_erf(w[6]), gelu_erf(w[7]));
             *reinterpret_cast<uint4*>(dst) = o;
           } else {
-            const float4 r0 = res[2 * g], r1 = res[2 * g + 1];
+            const float4 r0 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g];
+            const float4 r1 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g + 1];
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
                                                     (int64_t)row * p.ld_out + n);
             dst[0] = make_float4(w[0] + r0.x, w[1] + r0.y, w[2] + r0.z, w[3] + r0.w);
@@ -369,7 +373,7 @@ static int launch_gemm_t(const GemmArgs& a, const GemmKernelParams& kp, cudaStre
   const int max_tiles = ((a.rows_max + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
   const int grid = max_tiles < num_sms ? max_tiles : num_sms;
   if (grid <= 0) return TJ_OK;
-  gemm_tcgen05_kernel<BN, EPI><<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(ta, tb, kp);
+  gemm_tcgen05_kernel<BN, EPI><<<grid, gemm_threads_for(EPI), Cfg::kSmemBytes, stream>>>(ta, tb, kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
   return TJ_OK;

@@ -21,19 +21,22 @@
 namespace tj {
 
 // ---------------------------------------------------------------------------
-// Token plan: one CTA of 1024 threads.  Thread t owns a contiguous chunk of
-// the B*S mask bytes; a block-wide exclusive scan of the per-chunk valid
-// counts gives each chunk its first compact row.
+// Token plan: one CTA of 1024 threads = 32 warps.  Warp w owns a contiguous
+// segment of the B*S mask bytes and reads it 32 bytes at a time (coalesced);
+// a ballot gives the valid lanes, popc their rank.  Pass 1 counts each
+// segment, a scan of the 32 counts gives each warp its first compact row, and
+// pass 2 re-reads the segment and writes orig/inv/cu coalesced.
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 
 __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t* __restrict__ mask,
                                                                   int B, int S,
                                                                   int32_t* __restrict__ plan) {
-  const int64_t total = (int64_t)B * S;
-  const int64_t chunk = (total + kPlanThreads - 1) / kPlanThreads;
-  const int64_t begin = min(total, (int64_t)threadIdx.x * chunk);
-  const int64_t end = min(total, begin + chunk);
+  const int total = B * S;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int seg = ((total + 31) / 32 + 31) / 32 * 32;  // multiple of 32 elements
+  const int begin = min(total, warp * seg);
+  const int end = min(total, begin + seg);
 
   int32_t* cu = plan + 1;
   int32_t* cnt = plan + 2 + B;
@@ -41,61 +44,56 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
   int32_t* inv = orig + total;
 
   int count = 0;
-  if (mask == nullptr) {
-    count = (int)(end - begin);
-  } else {
-    for (int64_t i = begin; i < end; ++i) count += mask[i] != 0;
+  for (int i = begin + lane; i - lane < end; i += 32) {
+    const bool valid = i < end && (mask == nullptr || mask[i] != 0);
+    count += __popc(__ballot_sync(0xffffffffu, valid));
   }
-
-  // Block exclusive scan (warp shuffles, then a scan of the 32 warp totals).
-  __shared__ int warp_tot[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl = count;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) warp_tot[warp] = incl;
+  __shared__ int warp_base[32];
+  if (lane == 0) warp_base[warp] = count;
   __syncthreads();
   if (warp == 0) {
-    int w = warp_tot[lane];
-    int wi = w;
+    const int w = warp_base[lane];
+    int incl = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      int v = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += v;
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
     }
-    warp_tot[lane] = wi - w;  // exclusive prefix of warp totals
+    warp_base[lane] = incl - w;
+    if (lane == 31) {
+      plan[0] = incl;
+      cu[B] = incl;
+    }
   }
   __syncthreads();
-  int run = warp_tot[warp] + incl - count;
-
-  for (int64_t i = begin; i < end; ++i) {
-    if (i % S == 0) cu[i / S] = run;
-    const bool valid = (mask == nullptr) || mask[i] != 0;
-    if (valid) {
-      orig[run] = (int32_t)i;
-      inv[i] = run;
-      ++run;
-    } else {
-      inv[i] = -1;
+  int run = warp_base[warp];
+  int next_start = (begin + S - 1) / S * S;  // first sample start at or after `begin`
+  for (int i = begin + lane; i - lane < end; i += 32) {
+    const bool in = i < end;
+    const bool valid = in && (mask == nullptr || mask[i] != 0);
+    const unsigned bal = __ballot_sync(0xffffffffu, valid);
+    const int rank = __popc(bal & ((1u << lane) - 1u));
+    // Samples starting inside this 32-element group (several when S < 32).
+    const int group0 = i - lane;
+    while (next_start < group0 + 32 && next_start < end) {
+      const int k = next_start - group0;  // lane holding the sample start
+      if (lane == k) cu[next_start / S] = run + rank;
+      next_start += S;
     }
-  }
-  // The thread owning the last element publishes the total.
-  if (end == total && begin < end) {
-    cu[B] = run;
-    plan[0] = run;
-  }
-  if (total == 0 && threadIdx.x == 0) {
-    cu[B] = 0;
-    plan[0] = 0;
+    if (in) {
+      if (valid) {
+        orig[run + rank] = i;
+        inv[i] = run + rank;
+      } else {
+        inv[i] = -1;
+      }
+    }
+    run += __popc(bal);
   }
   __syncthreads();
   __threadfence_block();
-  for (int b = threadIdx.x; b < B; b += kPlanThreads) {
+  for (int b = threadIdx.x; b < B; b += kPlanThreads)
     cnt[b] = ((volatile int32_t*)cu)[b + 1] - ((volatile int32_t*)cu)[b];
-  }
 }
 
 int64_t plan_ints(int B, int S) { return 2 + 2 * (int64_t)B + 2 * (int64_t)B * S; }

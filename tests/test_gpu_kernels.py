@@ -35,7 +35,7 @@ def _plan_reference(mask):
     return orig, inv, counts, cu
 
 
-@pytest.mark.parametrize("B,S", [(1, 1), (2, 8), (3, 1000), (8, 2048), (1, 131072)])
+@pytest.mark.parametrize("B,S", [(1, 1), (2, 8), (40, 7), (33, 33), (3, 1000), (8, 2048), (1, 131072)])
 def test_token_plan(cuda_pkg, B, S):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(B * 7 + S)
