@@ -1,0 +1,94 @@
+"""Worker for tests/test_gpu_multi.py, launched with torchrun (one rank per GPU).
+
+Checks, on N GPUs over NCCL:
+  * batch sharding: each rank runs its balanced range of the batch; the
+    gathered output is bit-identical to the whole batch on one GPU;
+  * context parallelism: one sequence split into valid-token balanced chunks,
+    K/V all-gathered every layer; the gathered output passes the reference's
+    strict gate against the single-GPU model (non-causal one layer, and
+    causal two layers).
+Exits non-zero on any failure.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+import __graft_entry__  # noqa: E402
+import oracle  # noqa: E402
+
+
+def main() -> int:
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    pkg = __graft_entry__.load_package()
+    from techjam_b200 import sharding
+
+    pkg._lib.set_sync_check(True)
+    failures = []
+
+    def model_for(cfg, sd):
+        m = pkg.UserOptimizedTransformer(pkg.TransformerConfig(*cfg.__dict__.values()))
+        m.load_state_dict(sd, strict=True)
+        return m.to(dev).eval()
+
+    with torch.inference_mode():
+        # ---- batch sharding ------------------------------------------------
+        cfg = oracle.TransformerConfig(6, 512, 1024, 16, 4096, 1, False)
+        sd = oracle.make_state_dict(cfg, seed=5)
+        x, mask = oracle.generate_random_case(cfg, seed=5, padding_ratio=0.5)
+        model = model_for(cfg, sd)
+        a, b = sharding.batch_ranges(cfg.batch_size, world)[rank]
+        bs = sharding.BatchShardedEncoder(model)
+        out = bs.forward(x[a:b].to(dev), mask[a:b].to(dev), gather=True)
+        full = model(x.to(dev), mask.to(dev))
+        if not torch.equal(out, full):
+            failures.append(f"batch sharding differs from one GPU: {float((out - full).abs().max())}")
+
+        # ---- context parallelism -------------------------------------------
+        for cfg_t, pad in (((1, 4096, 1024, 16, 4096, 1, False), 0.1), ((1, 3000, 512, 8, 1024, 2, True), 0.2)):
+            cfg = oracle.TransformerConfig(*cfg_t)
+            sd = oracle.make_state_dict(cfg, seed=7)
+            x, mask = oracle.generate_random_case(cfg, seed=7, padding_ratio=pad)
+            model = model_for(cfg, sd)
+            ranges = sharding.sequence_ranges(mask[0], world)
+            slab = max(e - s for s, e in ranges)
+            s0, e0 = ranges[rank]
+            cp = sharding.ContextParallelEncoder(model)
+            out_local = cp.forward(x[:, s0:e0].contiguous().to(dev), mask[:, s0:e0].contiguous().to(dev), slab)
+            padded = torch.zeros(1, slab, cfg.d_model, device=dev)
+            padded[:, : e0 - s0] = out_local
+            parts = [torch.empty_like(padded) for _ in range(world)]
+            dist.all_gather(parts, padded)
+            out = torch.cat([parts[r][:, : e - s] for r, (s, e) in enumerate(ranges)], dim=1)
+            ref = model(x.to(dev), mask.to(dev))
+            r = oracle.compare_outputs(ref.cpu(), out.cpu())
+            if not r.passed:
+                failures.append(f"context parallel {cfg_t}: {r}")
+            if torch.count_nonzero(out.cpu()[~mask]) != 0:
+                failures.append(f"context parallel {cfg_t}: padded rows not zero")
+        pkg._lib.device_status(torch.cuda.current_stream().cuda_stream)
+
+    dist.barrier(device_ids=[local])
+    dist.destroy_process_group()
+    if failures:
+        print(f"rank {rank} FAILED:\n" + "\n".join(failures), flush=True)
+        return 1
+    print(f"rank {rank} OK", flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

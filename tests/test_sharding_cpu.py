@@ -1,0 +1,153 @@
+"""Host-side multi-GPU logic on CPU: shard ranges, and the context-parallel
+decomposition run by two gloo ranks.
+
+The gloo test mirrors what ContextParallelEncoder does on GPUs -- valid-token
+balanced chunks, compact local K/V padded to a common slab,
+all_gather_into_tensor into [G][2][H][slab][dh], key-segment tables from
+`segment_metadata`, attention walking the segments in order -- with the
+oracle's FP32 math in place of the kernels, and checks each rank's queries
+against the oracle's full-sequence attention.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle
+
+
+def test_batch_ranges(pkg):
+    from techjam_b200 import sharding
+
+    for batch in (0, 1, 7, 8, 32, 33):
+        for world in (1, 2, 3, 8):
+            r = sharding.batch_ranges(batch, world)
+            assert len(r) == world and r[0][0] == 0 and r[-1][1] == batch
+            assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+            sizes = [e - s for s, e in r]
+            assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_sequence_ranges_balance_valid_tokens(pkg, world):
+    from techjam_b200 import sharding
+
+    g = torch.Generator().manual_seed(world)
+    for S in (1, 100, 4096):
+        for kind in ("prefix", "random", "none", "empty"):
+            if kind == "prefix":
+                valid = torch.arange(S) < int(torch.randint(1, S + 1, (1,), generator=g))
+            elif kind == "random":
+                valid = torch.rand(S, generator=g) < 0.6
+            elif kind == "none":
+                valid = torch.ones(S, dtype=torch.bool)
+            else:
+                valid = torch.zeros(S, dtype=torch.bool)
+            r = sharding.sequence_ranges(valid, world)
+            assert len(r) == world and r[0][0] == 0 and r[-1][1] == S
+            assert all(a[1] == b[0] and a[0] <= a[1] for a, b in zip(r, r[1:]))
+            counts = [int(valid[s:e].sum()) for s, e in r]
+            assert max(counts) - min(counts) <= 1, (kind, S, counts)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _project(sd, p, x, name):
+    return torch.nn.functional.linear(x, sd[p + name + ".weight"], sd[p + name + ".bias"])
+
+
+def _cp_rank(rank, world, port, causal, result_q):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import __graft_entry__
+
+        __graft_entry__.load_package()
+        from techjam_b200 import sharding
+
+        cfg = oracle.TransformerConfig(1, 300, 64, 2, 128, 1, causal)
+        sd = oracle.make_state_dict(cfg, seed=11)
+        x, mask = oracle.generate_random_case(cfg, seed=11, padding_ratio=0.3)
+        mask[0, 40:47] = False  # a hole inside the valid prefix
+        H, D = cfg.num_heads, cfg.d_model
+        dh = D // H
+        ranges = sharding.sequence_ranges(mask[0], world)
+        a, b = ranges[rank]
+        slab = max(e - s for s, e in ranges)
+        p = "layers.0."
+        h = torch.nn.functional.layer_norm(x, (D,), sd[p + "norm1.weight"], sd[p + "norm1.bias"], 1e-5)[0]
+        # Compact local valid tokens, as the token plan orders them.
+        local_valid = torch.nonzero(mask[0, a:b]).flatten() + a
+        n_local = local_valid.numel()
+        hl = h[local_valid]
+        q = _project(sd, p, hl, "attention.q_proj").view(n_local, H, dh).transpose(0, 1)
+        k = _project(sd, p, hl, "attention.k_proj").view(n_local, H, dh).transpose(0, 1)
+        v = _project(sd, p, hl, "attention.v_proj").view(n_local, H, dh).transpose(0, 1)
+        slab_kv = torch.full((2, H, slab, dh), float("nan"))  # rows past the count stay garbage
+        slab_kv[0, :, :n_local] = k
+        slab_kv[1, :, :n_local] = v
+        kv_all = torch.empty(world, 2, H, slab, dh)
+        dist.all_gather_into_tensor(kv_all.view(-1), slab_kv.reshape(-1))
+        counts = torch.empty(world, dtype=torch.int32)
+        dist.all_gather_into_tensor(counts, torch.tensor([n_local], dtype=torch.int32))
+        kv_off, kv_len, q_pos0 = sharding.segment_metadata(counts, rank, causal)
+        # Walk the segments in order, as the attention kernel does.
+        ks, vs = [], []
+        for gidx in range(world):
+            o, l = int(kv_off[0, gidx]), int(kv_len[0, gidx])
+            ks.append(kv_all[gidx, 0, :, o : o + l])
+            vs.append(kv_all[gidx, 1, :, o : o + l])
+        kk, vv = torch.cat(ks, 1), torch.cat(vs, 1)
+        s = torch.matmul(q, kk.transpose(-1, -2)) * dh**-0.5
+        if causal:
+            qp = int(q_pos0[0]) + torch.arange(n_local)[:, None]
+            kp = torch.arange(kk.shape[1])[None, :]
+            s = s.masked_fill(kp > qp, float("-inf"))
+        ctx = torch.matmul(torch.softmax(s, -1), vv).transpose(0, 1).reshape(n_local, D)
+
+        # Oracle: full-sequence attention context for the same query rows.
+        full_valid = torch.nonzero(mask[0]).flatten()
+        qf = _project(sd, p, h, "attention.q_proj").view(300, H, dh).transpose(0, 1)
+        kf = _project(sd, p, h, "attention.k_proj").view(300, H, dh).transpose(0, 1)
+        vf = _project(sd, p, h, "attention.v_proj").view(300, H, dh).transpose(0, 1)
+        sf = torch.matmul(qf, kf.transpose(-1, -2)) * dh**-0.5
+        if causal:
+            sf = sf.masked_fill(torch.ones(300, 300, dtype=torch.bool).triu(1), float("-inf"))
+        sf = sf.masked_fill(~mask[0][None, None, :], float("-inf"))
+        ref = torch.matmul(torch.softmax(sf, -1), vf).transpose(0, 1).reshape(300, D)[local_valid]
+        assert set(full_valid.tolist()) >= set(local_valid.tolist())
+        err = float((ctx - ref).abs().max()) if n_local else 0.0
+        result_q.put((rank, n_local, err, None))
+    except Exception as e:  # report to the parent instead of hanging it
+        result_q.put((rank, -1, float("inf"), repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_context_parallel_decomposition_two_gloo_ranks(pkg, causal):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cp_rank, args=(r, world, port, causal, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, n_local, err, exc in sorted(results):
+        assert exc is None, f"rank {rank}: {exc}"
+        assert n_local > 0
+        assert err < 1e-5, f"rank {rank}: max abs error {err}"
