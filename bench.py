@@ -366,27 +366,65 @@ def run_ours(args, world, rank, local):
 
 
 def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
-    """Same metric through the public API with host buffers: pinned x -> device,
-    forward, output -> pinned host, every step inside the timed region."""
-    x_host = x_cpu.pin_memory()
-    m_host = mask_cpu.pin_memory()
-    out_host = torch.empty_like(x_cpu).pin_memory()
+    """Same metric through the public API with host buffers: every step copies
+    its input from pinned host memory to the device, runs the forward and
+    copies the output back to pinned host memory, all inside the timed region.
+    Steps are pipelined the way a serving loop runs them: the upload of step
+    i+1 and the download of step i-1 (two copy streams) overlap the forward of
+    step i (compute stream), with events ordering each step's three stages."""
     steps = max(3, min(args.steps, 30))
-    stream = torch.cuda.current_stream(device)
+    nbuf = 3
+    x_host = [x_cpu.clone().pin_memory() for _ in range(nbuf)]
+    m_host = mask_cpu.pin_memory()
+    out_host = [torch.empty_like(x_cpu).pin_memory() for _ in range(nbuf)]
+    x_dev = [torch.empty_like(x_cpu, device=device) for _ in range(nbuf)]
+    m_dev = [torch.empty_like(mask_cpu, device=device) for _ in range(nbuf)]
+    outs = [None] * nbuf
+    compute = torch.cuda.current_stream(device)
+    h2d = torch.cuda.Stream(device)
+    d2h = torch.cuda.Stream(device)
+    up_done = [torch.cuda.Event() for _ in range(nbuf)]
+    fwd_done = [torch.cuda.Event() for _ in range(nbuf)]
+    down_done = [torch.cuda.Event() for _ in range(nbuf)]
+
+    def run(n):
+        for i in range(n + 2):
+            if i < n:  # upload step i
+                b = i % nbuf
+                h2d.wait_event(fwd_done[b])  # buffer b's previous forward has read x_dev[b]
+                with torch.cuda.stream(h2d):
+                    x_dev[b].copy_(x_host[b], non_blocking=True)
+                    m_dev[b].copy_(m_host, non_blocking=True)
+                up_done[b].record(h2d)
+            if 1 <= i <= n:  # forward step i-1
+                b = (i - 1) % nbuf
+                compute.wait_event(up_done[b])
+                compute.wait_event(down_done[b])  # at most nbuf steps in flight
+                outs[b] = model(x_dev[b], m_dev[b])
+                fwd_done[b].record(compute)
+            if i >= 2:  # download step i-2
+                b = (i - 2) % nbuf
+                d2h.wait_event(fwd_done[b])
+                with torch.cuda.stream(d2h):
+                    out_host[b].copy_(outs[b], non_blocking=True)
+                outs[b].record_stream(d2h)
+                down_done[b].record(d2h)
+
     with torch.inference_mode():
-        for _ in range(2):
-            out_host.copy_(model(x_host.to(device, non_blocking=True), m_host.to(device, non_blocking=True)),
-                           non_blocking=True)
+        for e in down_done + fwd_done:
+            e.record(compute)
+        run(3)
         torch.cuda.synchronize(device)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier(world, device)
         torch.cuda.synchronize(device)
-        start.record(stream)
-        for _ in range(steps):
-            xd = x_host.to(device, non_blocking=True)
-            md = m_host.to(device, non_blocking=True)
-            out_host.copy_(model(xd, md), non_blocking=True)
-        end.record(stream)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(compute)
+        h2d.wait_stream(compute)
+        d2h.wait_stream(compute)
+        run(steps)
+        compute.wait_stream(d2h)
+        compute.wait_stream(h2d)
+        end.record(compute)
         torch.cuda.synchronize(device)
     ms = max_over_ranks(world, start.elapsed_time(end), device) / steps
     B, S, _ = x_cpu.shape
@@ -397,6 +435,7 @@ def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
         "steps": steps,
         "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
         "d2h_bytes_per_step": x_cpu.numel() * 4,
+        "pipeline": "upload i+1 / forward i / download i-1 overlapped on 3 streams",
     }
 
 

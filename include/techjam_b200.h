@@ -25,7 +25,8 @@
  *   mask            uint8/bool [B, S], nonzero = valid token (may be NULL)
  *   weights         float16 [N, K] (nn.Linear layout), biases float32 [N]
  *   LayerNorm       gamma/beta float32 [D], eps as given (nn.LayerNorm: 1e-5)
- *   qkv (head-major) float16 [3][H][rows][64]
+ *   qkv (head-major) float16 [3][H][rows][64]; a head dim below 64 is stored
+ *                   zero-padded to 64 (head dims above 64 are not supported)
  *   ctx             float16 [rows][D]
  *   "compact rows"  the valid tokens of the batch packed densely in
  *                   (sample, position) order, as the token plan defines.
@@ -130,14 +131,14 @@ TJ_API int tj_gemm_bias_gelu_f16(const void* a16, const void* w16, const float* 
                           const int32_t* row_count, int rows_max, int n, int k, void* out16,
                           void* stream);
 
-/* Masked multi-head attention over compact rows, head_dim 64.
- *   q16       [H][q_rows][64]
+/* Masked multi-head attention over compact rows, head_dim 1..64.
+ *   q16       [H][q_rows][64] (head_dim values then zeros up to 64)
  *   k16, v16  addressed as [G][H][kv_rows][64] with element strides
  *             kv_stride_h (between heads) and kv_stride_g (between segments)
  *   q_cu      [batch+1]: queries of sample b are q rows [q_cu[b], q_cu[b+1])
  *   kv_off, kv_len [batch*G]: keys of sample b are, for g = 0..G-1 in order,
  *             rows [kv_off[b*G+g], +kv_len[b*G+g]) of segment g
- *   ctx16     [q_rows][H*64]: softmax(q k^T * scale) v per head
+ *   ctx16     [q_rows][H*head_dim]: softmax(q k^T * scale) v per head
  *   causal    mask keys whose position (order within the sample's keys) is
  *             after the query position q_pos0[b] + (row - q_cu[b]);
  *             q_pos0 may be NULL (= 0) when G == 1.

@@ -64,6 +64,7 @@ struct AttnKernelParams {
   const int32_t* q_pos0;
   __half* ctx;
   int ld_ctx;
+  int dh_out;  // real head dim (<= 64): columns of ctx written per head
 };
 
 // Walks the key tiles of one sample in order: segment g, tile i inside it.
@@ -486,7 +487,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int d = 0; d < 32; ++d) o0[d] = o1[d] = 0u;
         }
-        if (q_local < nq) {
+        if (q_local < nq && p.dh_out != kDH) {
+          // Head dim below 64: the padded columns are dropped.
+          __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * p.dh_out;
+#pragma unroll
+          for (int d = 0; d < 32; ++d)
+            if (d < p.dh_out) dst[d] = __float2half_rn(__uint_as_float(o0[d]) * inv_l);
+#pragma unroll
+          for (int d = 0; d < 32; ++d)
+            if (32 + d < p.dh_out) dst[32 + d] = __float2half_rn(__uint_as_float(o1[d]) * inv_l);
+        } else if (q_local < nq) {
           __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * kDH;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -520,8 +530,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 int launch_attention(const AttnArgs& a, cudaStream_t stream) {
-  if (a.head_dim != kDH)
-    return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: head_dim %d (only 64 is built)", a.head_dim);
+  if (a.head_dim <= 0 || a.head_dim > kDH)
+    return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: head_dim %d (1..64 supported)", a.head_dim);
   if (a.H <= 0 || a.B <= 0 || a.G <= 0 || a.q_rows < 0 || a.kv_rows < 0 || a.max_q_per_sample < 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: bad sizes H=%d B=%d G=%d", a.H, a.B, a.G);
   if (!a.q || !a.k || !a.v || !a.ctx || !a.q_cu || !a.kv_off || !a.kv_len)
@@ -581,7 +591,8 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   kp.causal = a.causal;
   kp.q_pos0 = a.q_pos0;
   kp.ctx = static_cast<__half*>(a.ctx);
-  kp.ld_ctx = a.H * kDH;
+  kp.ld_ctx = a.H * a.head_dim;
+  kp.dh_out = a.head_dim;
   dim3 grid((a.max_q_per_sample + 2 * kAttnBM - 1) / (2 * kAttnBM), a.H, a.B);
   if (grid.y > 65535 || grid.z > 65535)
     return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d or B=%d above 65535", a.H, a.B);

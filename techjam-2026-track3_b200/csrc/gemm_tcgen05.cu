@@ -36,6 +36,7 @@ __host__ __device__ constexpr int epi_warps_for(int epi) { return epi == 1 ? 8 :
 __host__ __device__ constexpr int gemm_threads_for(int epi) { return 64 + 32 * epi_warps_for(epi); }
 constexpr int kBM = 128;
 constexpr int kBK = 64;
+constexpr int kHeadPad = 64;  // head-major row length (halves) of the QKV output
 
 struct GemmKernelParams {
   const float* bias;
@@ -253,18 +254,37 @@ __global__ void __launch_bounds__(gemm_threads_for(EPI), 1)
                         __uint_as_float(r[8 * g + 4]) + b1.x, __uint_as_float(r[8 * g + 5]) + b1.y,
                         __uint_as_float(r[8 * g + 6]) + b1.z, __uint_as_float(r[8 * g + 7]) + b1.w};
           if (EPI == kEpiQkvHeadMajor) {
-            const int which = n / p.d_model;
-            const int rem = n - which * p.d_model;
-            const int h = rem / p.head_dim;
-            const int d = rem - h * p.head_dim;
-            __half* dst = static_cast<__half*>(p.out) +
-                          (((int64_t)(which * p.heads + h) * p.rows_max + row) * p.head_dim + d);
-            uint4 o;
-            o.x = pack_half2(w[0], w[1]);
-            o.y = pack_half2(w[2], w[3]);
-            o.z = pack_half2(w[4], w[5]);
-            o.w = pack_half2(w[6], w[7]);
-            *reinterpret_cast<uint4*>(dst) = o;
+            // Head-major rows are kHeadPad (64) halves; a head dim below 64 is
+            // stored zero-padded, so attention always sees 64-wide rows.
+            __half* qkv = static_cast<__half*>(p.out);
+            if ((p.head_dim & 7) == 0) {
+              const int which = n / p.d_model;
+              const int rem = n - which * p.d_model;
+              const int h = rem / p.head_dim;
+              const int d = rem - h * p.head_dim;
+              __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
+              uint4 o;
+              o.x = pack_half2(w[0], w[1]);
+              o.y = pack_half2(w[2], w[3]);
+              o.z = pack_half2(w[4], w[5]);
+              o.w = pack_half2(w[6], w[7]);
+              *reinterpret_cast<uint4*>(rowp + d) = o;
+              if (d + 8 == p.head_dim)
+                for (int z = p.head_dim; z < kHeadPad; z += 8)
+                  *reinterpret_cast<uint4*>(rowp + z) = make_uint4(0u, 0u, 0u, 0u);
+            } else {
+              for (int e = 0; e < 8; ++e) {
+                const int ne = n + e;
+                const int which = ne / p.d_model;
+                const int rem = ne - which * p.d_model;
+                const int h = rem / p.head_dim;
+                const int d = rem - h * p.head_dim;
+                __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
+                rowp[d] = __float2half_rn(w[e]);
+                if (d + 1 == p.head_dim)
+                  for (int z = p.head_dim; z < kHeadPad; ++z) rowp[z] = __float2half_rn(0.f);
+              }
+            }
           } else if (EPI == kEpiGeluF16) {
             __half* dst = static_cast<__half*>(p.out) + (int64_t)row * p.ld_out + n;
             uint4 o;
@@ -405,10 +425,10 @@ int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
   kp.head_dim = a.head_dim;
   switch (epilogue) {
     case kEpiQkvHeadMajor:
-      if (a.heads <= 0 || a.head_dim <= 0 || a.head_dim % 8 != 0 || a.N != 3 * a.heads * a.head_dim)
+      if (a.heads <= 0 || a.head_dim <= 0 || a.head_dim > kHeadPad || a.N != 3 * a.heads * a.head_dim)
         return set_error(TJ_ERR_UNSUPPORTED,
-                         "gemm_qkv_headmajor: N=%d must be 3*H*dh with dh %% 8 == 0 (H=%d dh=%d)",
-                         a.N, a.heads, a.head_dim);
+                         "gemm_qkv_headmajor: N=%d must be 3*H*dh with dh <= %d (H=%d dh=%d)",
+                         a.N, kHeadPad, a.heads, a.head_dim);
       kp.d_model = a.heads * a.head_dim;
       return launch_gemm_t<256, kEpiQkvHeadMajor>(a, kp, stream);
     case kEpiResidualF32:

@@ -105,9 +105,9 @@ def gemm_qkv_headmajor(a16, w_qkv16, b_qkv, num_heads, row_count=None, out=None)
     rows, D = a16.shape
     if w_qkv16.shape != (3 * D, D):
         raise ValueError(f"w_qkv16 must be [{3 * D}, {D}], got {tuple(w_qkv16.shape)}")
-    dh = D // num_heads
     if out is None:
-        out = torch.empty(3, num_heads, rows, dh, dtype=torch.float16, device=dev)
+        # head-major, each head zero-padded to 64 halves
+        out = torch.empty(3, num_heads, rows, 64, dtype=torch.float16, device=dev)
     lib = _lib.load()
     rc = lib.tj_gemm_qkv_headmajor(
         a16.data_ptr(), w_qkv16.data_ptr(), b_qkv.data_ptr(), _ptr(row_count), rows, D, num_heads,
@@ -159,19 +159,21 @@ def gemm_bias_gelu_f16(a16, w16, bias, row_count=None, out=None):
 
 
 def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causal=False,
-                   q_pos0=None, out=None):
-    """q: [H, q_rows, 64]; k, v: [G, H, kv_rows, 64] (any strides with unit inner stride);
-    q_cu: [B+1]; kv_off/kv_len: [B, G] int32.  Returns ctx [q_rows, H*64] fp16."""
+                   q_pos0=None, out=None, head_dim=64):
+    """q: [H, q_rows, 64]; k, v: [G, H, kv_rows, 64] (any strides with unit inner stride;
+    rows hold head_dim values then zeros up to 64); q_cu: [B+1]; kv_off/kv_len: [B, G]
+    int32.  Returns ctx [q_rows, H*head_dim] fp16."""
     dev = q.device
     _require(q, "q", torch.float16, dev)
     if k.dim() == 3:
         k = k.unsqueeze(0)
         v = v.unsqueeze(0)
-    G, H, kv_rows, dh = k.shape
-    if q.shape[0] != H or q.shape[2] != dh:
-        raise ValueError("q must be [H, q_rows, head_dim] matching k")
-    if k.stride() != v.stride() or k.stride(-1) != 1 or k.stride(-2) != dh:
-        raise ValueError("k and v must share strides with contiguous [rows, head_dim] slabs")
+    G, H, kv_rows, row = k.shape
+    if row != 64 or q.shape[0] != H or q.shape[2] != 64:
+        raise ValueError("q, k, v rows must be 64 halves (head dims below 64 zero-padded)")
+    if k.stride() != v.stride() or k.stride(-1) != 1 or k.stride(-2) != 64:
+        raise ValueError("k and v must share strides with contiguous [rows, 64] slabs")
+    dh = head_dim
     B = q_cu.numel() - 1
     if out is None:
         out = torch.empty(q.shape[1], H * dh, dtype=torch.float16, device=dev)

@@ -147,8 +147,8 @@ class ContextParallelEncoder:
         kv_off, kv_len, q_pos0 = segment_metadata(counts, self.rank, bool(cfg.causal))
 
         a16 = torch.empty(slab, D, dtype=torch.float16, device=dev)
-        qkv = torch.empty(3, H, slab, dh, dtype=torch.float16, device=dev)
-        kv_all = torch.empty(self.world, 2, H, slab, dh, dtype=torch.float16, device=dev)
+        qkv = torch.empty(3, H, slab, 64, dtype=torch.float16, device=dev)  # heads padded to 64
+        kv_all = torch.empty(self.world, 2, H, slab, 64, dtype=torch.float16, device=dev)
         ctx = torch.empty(slab, D, dtype=torch.float16, device=dev)
         h16 = torch.empty(slab, F, dtype=torch.float16, device=dev)
 
@@ -166,7 +166,7 @@ class ContextParallelEncoder:
                                        row_count=nv, out=qkv)
             dist.all_gather_into_tensor(kv_all.view(-1), qkv[1:3].reshape(-1), group=self.group)
             kernels.flash_attn_fwd(qkv[0], kv_all[:, 0], kv_all[:, 1], cu, kv_off, kv_len, Sl, att.scale,
-                                   causal=bool(cfg.causal), q_pos0=q_pos0, out=ctx)
+                                   causal=bool(cfg.causal), q_pos0=q_pos0, out=ctx, head_dim=dh)
             kernels.gemm_bias_residual_f32(ctx, att._out_weight_mixed, att.out_proj.bias, xin,
                                            resid_map=in_map, row_count=nv, out=x1)
             kernels.ln_cast_f16(x1, layer.norm2.weight, layer.norm2.bias, layer.norm2.eps, row_count=nv,

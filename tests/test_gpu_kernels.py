@@ -91,21 +91,29 @@ def _gemm_ref(a16, w16, bias):
     return a16.float() @ w16.float().t() + bias
 
 
-@pytest.mark.parametrize("rows,count,D,H", [(128, 128, 256, 4), (1000, 777, 768, 12), (4096, 4096, 1024, 16), (300, 0, 256, 4)])
+@pytest.mark.parametrize(
+    "rows,count,D,H",
+    [(128, 128, 256, 4), (1000, 777, 768, 12), (4096, 4096, 1024, 16), (300, 0, 256, 4),
+     (200, 150, 256, 8), (40, 33, 16, 4), (77, 77, 96, 4)],
+)
 def test_gemm_qkv_headmajor(cuda_pkg, rows, count, D, H):
+    """Head-major output [3][H][rows][64]; head dims below 64 zero-padded."""
     k = cuda_pkg.kernels
+    dh = D // H
     g = torch.Generator().manual_seed(rows + D)
     a = torch.randn(rows, D, generator=g).half().to(DEV)
     w = (torch.randn(3 * D, D, generator=g) / math.sqrt(D)).half().to(DEV)
     b = torch.randn(3 * D, generator=g).to(DEV)
-    out = torch.full((3, H, rows, D // H), float("nan"), dtype=torch.float16, device=DEV)
+    out = torch.full((3, H, rows, 64), float("nan"), dtype=torch.float16, device=DEV)
     k.gemm_qkv_headmajor(a, w, b, H, row_count=torch.tensor([count], dtype=torch.int32, device=DEV), out=out)
     ref = _gemm_ref(a, w, b)  # [rows, 3D]
-    ref_hm = ref.view(rows, 3, H, D // H).permute(1, 2, 0, 3)
-    got = out[:, :, :count].float()
+    ref_hm = ref.view(rows, 3, H, dh).permute(1, 2, 0, 3)
+    got = out[:, :, :count, :dh].float()
     exp = ref_hm[:, :, :count]
     # fp32 accumulation of fp16 products, then one fp16 rounding.
     assert torch.all((got - exp).abs() <= exp.abs() * 2**-10 + 2e-3), float((got - exp).abs().max())
+    if dh < 64:
+        assert torch.count_nonzero(out[:, :, :count, dh:].float()) == 0, "head padding must be zero"
     if count < rows:
         assert torch.isnan(out[:, :, count:].float()).all(), "rows past the count must not be written"
 
@@ -137,10 +145,11 @@ def test_gemm_bias_gelu_f16(cuda_pkg, rows, N, K):
     assert torch.all((out - ref).abs() <= ref.abs() * 2**-10 + 2e-3), float((out - ref).abs().max())
 
 
-def _attn_ref(q, k, v, q_cu, kv_off, kv_len, scale, causal=False):
+def _attn_ref(q, k, v, q_cu, kv_off, kv_len, scale, causal=False, dh=64):
     """q [H, rows, 64] fp16; k/v [G, H, rows, 64]; fp32 math per sample."""
     H = q.shape[0]
-    out = torch.zeros(q.shape[1], H * 64, dtype=torch.float32, device=q.device)
+    q, k, v = q[..., :dh], k[..., :dh], v[..., :dh]
+    out = torch.zeros(q.shape[1], H * dh, dtype=torch.float32, device=q.device)
     B = q_cu.numel() - 1
     G = k.shape[0]
     for b in range(B):
@@ -160,7 +169,7 @@ def _attn_ref(q, k, v, q_cu, kv_off, kv_len, scale, causal=False):
             kp = torch.arange(kk.shape[1], device=q.device)[None, :]
             s = s.masked_fill(kp > qp, float("-inf"))
         p = torch.softmax(s, dim=-1)
-        out[q0:q1] = torch.matmul(p, vv).transpose(0, 1).reshape(q1 - q0, H * 64)
+        out[q0:q1] = torch.matmul(p, vv).transpose(0, 1).reshape(q1 - q0, H * dh)
     return out
 
 
@@ -207,3 +216,23 @@ def test_flash_attention_segments(cuda_pkg):
     out = k.flash_attn_fwd(q, kk, vv, q_cu.to(DEV), kv_off.to(DEV), kv_len.to(DEV), q_rows, 0.125)
     ref = _attn_ref(q, kk, vv, q_cu, kv_off, kv_len, 0.125)
     assert float((out.float() - ref).abs().max()) < 4e-3
+
+
+@pytest.mark.parametrize("dh", [4, 8, 32])
+def test_flash_attention_small_heads(cuda_pkg, dh):
+    """Head dims below 64: rows zero-padded to 64, context holds dh columns per head."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(dh)
+    H = 4
+    lens = torch.tensor([300, 77], dtype=torch.int32)
+    cu = torch.tensor([0, 300, 377], dtype=torch.int32)
+    qkv = torch.zeros(3, H, 400, 64, dtype=torch.float16)
+    qkv[..., :dh] = torch.randn(3, H, 400, dh, generator=g).half()
+    qkv = qkv.to(DEV)
+    kv_off, kv_len = cu[:-1].view(-1, 1).contiguous(), lens.view(-1, 1).contiguous()
+    scale = dh**-0.5
+    out = k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu.to(DEV), kv_off.to(DEV), kv_len.to(DEV), 300, scale,
+                           head_dim=dh)
+    assert out.shape == (400, H * dh)
+    ref = _attn_ref(qkv[0], qkv[1:2], qkv[2:3], cu, kv_off, kv_len, scale, dh=dh)
+    assert float((out[:377].float() - ref[:377]).abs().max()) < 4e-3

@@ -52,6 +52,17 @@ def test_golden_cpu_plumbing_config(cuda_pkg, golden):
     assert torch.count_nonzero(out.cpu()[~mask]) == 0
 
 
+@pytest.mark.parametrize("name", ["mask_paths_causal0_mask0", "mask_paths_causal0_mask1",
+                                  "mask_paths_causal1_mask0", "mask_paths_causal1_mask1"])
+def test_golden_reference_unit_test_config(cuda_pkg, golden, name):
+    """The reference's own parity-test setup (tests/test_mask_paths.py: d_model 16,
+    4 heads of dim 4, FFN 16, 2 layers, causal x mask) against its stored outputs."""
+    e = golden[name]
+    cfg = oracle.TransformerConfig(*e["config"])
+    out = _run(_model(cuda_pkg, cfg, e["state_dict"]), e["x"], e["mask"])
+    _gate(e["out"], out, name)
+
+
 @pytest.mark.parametrize(
     "name",
     ["cfg1_trial1", "short_heavy_pad_b4_s128_d768", "dense_ln_b2_s512_d1024", "causal_two_layers_b2_s256",
