@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                              const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const AttnKernelParams p) {
   const int h = blockIdx.y, b = blockIdx.z;
+  pdl_wait();  // q/k/v and the token plan come from earlier kernels
   const int q_begin = p.q_cu[b];
   const int nq = p.q_cu[b + 1] - q_begin;
   const int q_tile0 = blockIdx.x * 2;
@@ -521,6 +522,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   }
 
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -596,8 +598,9 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   dim3 grid((a.max_q_per_sample + 2 * kAttnBM - 1) / (2 * kAttnBM), a.H, a.B);
   if (grid.y > 65535 || grid.z > 65535)
     return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d or B=%d above 65535", a.H, a.B);
-  attention_tcgen05_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tq, tk, tv, kp);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(attention_tcgen05_kernel, grid, dim3(kAttnThreads), kAttnSmem, stream, tq,
+                             tk, tv, kp);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return TJ_OK;
 }

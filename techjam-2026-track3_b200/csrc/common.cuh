@@ -66,6 +66,19 @@ __device__ __forceinline__ int warp_idx() {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of the library is launched with
+// programmatic stream serialization: it may start while its predecessor on the
+// stream is finishing, does its set-up (barriers, TMEM, descriptor prefetch),
+// and calls pdl_wait() before reading anything a predecessor wrote.  Each CTA
+// calls pdl_trigger() once its main work is done, so the successor is only
+// scheduled while the last CTAs drain.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -324,21 +337,21 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int a_mn, int
 // ~1e-38, which the caller rounds to fp16 zero).  Used for part of the
 // softmax exponentials so the MUFU unit and the FMA pipe share the load.
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer j
   x.x = fmaxf(x.x, -126.0f);
   x.y = fmaxf(x.y, -126.0f);
   const float2 t = fadd2(x, make_float2(kRound, kRound));
-  const float2 j = fadd2(t, make_float2(-kRound, -kRound));
-  const float2 r = fadd2(x, make_float2(-j.x, -j.y));
+  const float2 nj = ffma2(t, make_float2(-1.0f, -1.0f), make_float2(kRound, kRound));  // -j, exact
+  const float2 r = fadd2(x, nj);                                                      // x - j
   float2 p = make_float2(0.009569931775331497f, 0.009569931775331497f);
   p = ffma2(p, r, make_float2(0.0559174083173275f, 0.0559174083173275f));
   p = ffma2(p, r, make_float2(0.240247443318367f, 0.240247443318367f));
   p = ffma2(p, r, make_float2(0.6931218504905701f, 0.6931218504905701f));
   p = ffma2(p, r, make_float2(0.9999992847442627f, 0.9999992847442627f));
-  const int jx = __float_as_int(t.x) - 0x4B400000;
-  const int jy = __float_as_int(t.y) - 0x4B400000;
-  return make_float2(__int_as_float(__float_as_int(p.x) + (jx << 23)),
-                     __int_as_float(__float_as_int(p.y) + (jy << 23)));
+  // bits(t) = bits(kRound) + j and the low 9 bits of bits(kRound) are zero, so
+  // bits(t) << 23 == j << 23 (mod 2^32): add it to p's exponent field.
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 // max(a, b, c) in one instruction (three-input max of sm_100).

@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(gemm_threads_for(EPI), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the row count, A and the residual come from earlier kernels
 
   const int rows = p.row_count ? min(p.rows_max, *p.row_count) : p.rows_max;
   const int m_tiles = (rows + kBM - 1) / kBM;
@@ -313,6 +314,7 @@ __global__ void __launch_bounds__(gemm_threads_for(EPI), 1)
     }
   }
 
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -393,8 +395,9 @@ static int launch_gemm_t(const GemmArgs& a, const GemmKernelParams& kp, cudaStre
   const int max_tiles = ((a.rows_max + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
   const int grid = max_tiles < num_sms ? max_tiles : num_sms;
   if (grid <= 0) return TJ_OK;
-  gemm_tcgen05_kernel<BN, EPI><<<grid, gemm_threads_for(EPI), Cfg::kSmemBytes, stream>>>(ta, tb, kp);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(gemm_tcgen05_kernel<BN, EPI>, dim3(grid), dim3(gemm_threads_for(EPI)),
+                             Cfg::kSmemBytes, stream, ta, tb, kp);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
   return TJ_OK;
 }

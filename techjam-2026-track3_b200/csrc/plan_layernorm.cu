@@ -32,6 +32,7 @@ constexpr int kPlanThreads = 1024;
 __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t* __restrict__ mask,
                                                                   int B, int S,
                                                                   int32_t* __restrict__ plan) {
+  pdl_wait();
   const int total = B * S;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int seg = ((total + 31) / 32 + 31) / 32 * 32;  // multiple of 32 elements
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
   __threadfence_block();
   for (int b = threadIdx.x; b < B; b += kPlanThreads)
     cnt[b] = ((volatile int32_t*)cu)[b + 1] - ((volatile int32_t*)cu)[b];
+  pdl_trigger();
 }
 
 int64_t plan_ints(int B, int S) { return 2 + 2 * (int64_t)B + 2 * (int64_t)B * S; }
@@ -103,8 +105,8 @@ int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStre
   if ((int64_t)B * S > (int64_t)INT32_MAX - 1)
     return set_error(TJ_ERR_UNSUPPORTED, "token_plan: B*S=%lld exceeds int32", (long long)B * S);
   if (plan == nullptr) return set_error(TJ_ERR_INVALID_ARGUMENT, "token_plan: null plan buffer");
-  token_plan_kernel<<<1, kPlanThreads, 0, stream>>>(mask, B, S, plan);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(token_plan_kernel, dim3(1), dim3(kPlanThreads), 0, stream, mask, B, S, plan);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "token_plan launch: %s", cudaGetErrorString(e));
   return TJ_OK;
 }
@@ -144,6 +146,8 @@ __global__ void __launch_bounds__(256) ln_cast_f16_kernel(
     const float* __restrict__ beta, float eps, __half* __restrict__ y) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_trigger();
   const int limit = row_count ? min(rows, *row_count) : rows;
   if (row >= limit) return;
   const int64_t src = row_map ? (int64_t)row_map[row] : (int64_t)row;
@@ -180,6 +184,8 @@ __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__
                                                        float* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_trigger();
   if (row >= rows) return;
   const int64_t src = inv_map ? (int64_t)inv_map[row] : (int64_t)row;
   float4* orow = reinterpret_cast<float4*>(out + (int64_t)row * D);
@@ -243,13 +249,14 @@ int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* ro
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
   __half* y = static_cast<__half*>(y16);
+  cudaError_t e = cudaSuccess;
   switch (vpl) {
 #define TJ_LN_CASE(V) \
-  case V: ln_cast_f16_kernel<V><<<grid, warps * 32, 0, stream>>>(x, row_map, row_count, rows, D, gamma, beta, eps, y); break;
+  case V: e = launch_pdl(ln_cast_f16_kernel<V>, grid, dim3(warps * 32), 0, stream, x, row_map, row_count, rows, D, gamma, beta, eps, y); break;
     TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
 #undef TJ_LN_CASE
   }
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_cast_f16 launch: %s", cudaGetErrorString(e));
   return TJ_OK;
 }
@@ -266,13 +273,14 @@ int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, con
   if (rows == 0) return TJ_OK;
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
+  cudaError_t e = cudaSuccess;
   switch (vpl) {
 #define TJ_LN_CASE(V) \
-  case V: ln_final_kernel<V><<<grid, warps * 32, 0, stream>>>(x, inv_map, rows, D, gamma, beta, eps, out); break;
+  case V: e = launch_pdl(ln_final_kernel<V>, grid, dim3(warps * 32), 0, stream, x, inv_map, rows, D, gamma, beta, eps, out); break;
     TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
 #undef TJ_LN_CASE
   }
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_final_mask launch: %s", cudaGetErrorString(e));
   return TJ_OK;
 }
