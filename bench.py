@@ -49,6 +49,20 @@ WORKLOADS = {
              "long single sequence B=1 S=131072 d_model=1024 H=16 FFN=4096, L~U[0.9S,S]"),
 }
 
+# The reference's official test shapes (STATEMENT.md 3.7, tools/matrix_runner.py:49-64):
+# (id, batch, d_model, heads, seq_len, layers, ffn_dim), all causal, no padding.
+REFERENCE_SHAPES = (
+    (1, 64, 128, 4, 128, 4, 128), (2, 1, 128, 4, 128, 4, 128), (3, 4, 128, 4, 128, 4, 128),
+    (4, 16, 128, 4, 128, 4, 128), (5, 128, 128, 4, 128, 4, 128), (6, 10000, 128, 4, 128, 4, 128),
+    (7, 64, 32, 4, 128, 4, 32), (8, 64, 1024, 4, 128, 4, 1024), (9, 64, 128, 1, 128, 4, 128),
+    (10, 64, 128, 2, 128, 4, 128), (11, 64, 128, 16, 128, 4, 128), (12, 64, 128, 4, 32, 4, 128),
+    (13, 64, 128, 4, 1024, 4, 128), (14, 32, 1024, 16, 100000, 2, 1024),
+)
+for _sid, _b, _d, _h, _s, _l, _f in REFERENCE_SHAPES:
+    WORKLOADS[f"ref{_sid}"] = (_b, _s, _d, _h, _f, _l, True, 0.0, False,
+                               f"reference official shape #{_sid}: B={_b} S={_s} d_model={_d} H={_h} "
+                               f"FFN={_f} layers={_l} causal, no padding")
+
 PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -177,7 +191,9 @@ def algorithmic_work(cfg, mask):
     lens = mask.sum(1).double()
     D, F = cfg.d_model, cfg.ffn_dim
     nv = float(lens.sum())
-    attn = float((4.0 * lens * lens * D).sum())  # QK^T + PV, non-causal
+    attn = float((4.0 * lens * lens * D).sum())  # QK^T + PV
+    if cfg.causal:
+        attn = float((2.0 * lens * (lens + 1) * D).sum())  # the lower triangle
     gemm = nv * (8.0 * D * D + 4.0 * D * F)
     return nv, gemm * cfg.num_layers, attn * cfg.num_layers
 
@@ -269,6 +285,11 @@ def run_ours(args, world, rank, local):
 
     if args.workload == "long" and world > 1:
         return run_context_parallel(args, world, rank, local)
+    B_, S_, D_, H_ = WORKLOADS[args.workload][:4]
+    if D_ // H_ > 64:
+        return None if rank else {"metric": "layer-forward tokens/s", "impl": "ours",
+                                  "config": {"workload": WORKLOADS[args.workload][-1]},
+                                  "unsupported": f"head_dim {D_ // H_} (this build supports 1..64)"}
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     init_dist(world, "nccl")
@@ -282,7 +303,8 @@ def run_ours(args, world, rank, local):
     # Inputs larger than L2 between timed steps: x rotates over buffers whose
     # total exceeds the 126 MB L2 (and every step writes ~1 GB of activations).
     x_bytes = x_cpu.numel() * 4
-    n_rot = max(2, math.ceil(256e6 / x_bytes))
+    big = x_bytes > 2**31  # one input alone dwarfs L2; skip the extra copies and side measurements
+    n_rot = 1 if big else max(2, math.ceil(256e6 / x_bytes))
     xs = [x_cpu.to(device) for _ in range(n_rot)]
     stream = torch.cuda.current_stream(device)
 
@@ -312,17 +334,19 @@ def run_ours(args, world, rank, local):
     tokens_per_step = B * S * world
     value = tokens_per_step / (ms_step / 1e3)
 
-    e2e = measure_e2e(model, x_cpu, mask_cpu, device, args, world)
-    kernels = kernel_breakdown(pkg, model, cfg, xs[0], mask, device, args)
+    e2e = {"unavailable": "input larger than 2 GiB"} if big else measure_e2e(model, x_cpu, mask_cpu, device, args, world)
+    kernels = None if big else kernel_breakdown(pkg, model, cfg, xs[0], mask, device, args)
     nv, gemm_flops, attn_flops = algorithmic_work(cfg, mask_cpu)
 
     line = None
     if rank == 0:
         peaks, peak_kind = load_peaks()
-        roof = roofline(kernels, peaks, peak_kind)
+        roof = roofline(kernels, peaks, peak_kind) if kernels else None
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(args.workload, budget_s=args.cpu_budget)
+            cpu = ({"unavailable": "the FP32 oracle needs hours on the host for this shape"}
+                   if cfg.seq_len > 8192 or cfg.batch_size * cfg.seq_len > 1_000_000
+                   else cpu_baseline(args.workload, budget_s=args.cpu_budget))
         line = {
             "metric": "layer-forward tokens/s",
             "value": value,
@@ -444,6 +468,7 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
     buffers (CUDA events on the launching stream, averaged over repeats)."""
     k = pkg.kernels
     B, S, D, H, F = cfg.batch_size, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim
+    dh = D // H
     rows = B * S
     layer = model.layers[0]
     att = layer.attention
@@ -467,8 +492,9 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
         "gemm_qkv": (lambda: k.gemm_qkv_headmajor(a16, att._qkv_weight_mixed, att._qkv_bias_mixed, H,
                                                   row_count=nv_t, out=qkv), "tensor", 2.0 * nv * 3 * D * D),
         "flash_attn": (lambda: k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, kv_off.view(-1, 1),
-                                                cnt.view(-1, 1), S, 64**-0.5, out=ctx), "tensor",
-                       float((4.0 * lens * lens * D).sum())),
+                                                cnt.view(-1, 1), S, dh**-0.5, causal=bool(cfg.causal),
+                                                out=ctx, head_dim=dh), "tensor",
+                       float(((2.0 * lens * (lens + 1)) if cfg.causal else (4.0 * lens * lens)).mul(D).sum())),
         "gemm_out_resid": (lambda: k.gemm_bias_residual_f32(ctx, att._out_weight_mixed, att.out_proj.bias, xf,
                                                             resid_map=orig, row_count=nv_t, out=x1),
                            "tensor", 2.0 * nv * D * D),

@@ -146,8 +146,19 @@ def check(rc: int, op: str) -> None:
         raise TJError(op, rc, last_error())
 
 
+_sync_check = False
+
+
 def set_sync_check(enabled: bool) -> bool:
+    """Turns the library's per-call synchronise + device-status check on or
+    off (tests, debugging); returns the previous setting."""
+    global _sync_check
+    _sync_check = bool(enabled)
     return bool(load().tj_set_sync_check(1 if enabled else 0))
+
+
+def sync_check_enabled() -> bool:
+    return _sync_check
 
 
 def device_status(stream: int = 0) -> list[int]:

@@ -73,6 +73,12 @@ __device__ __forceinline__ int warp_idx() {
 // calls pdl_trigger() once its main work is done, so the successor is only
 // scheduled while the last CTAs drain.
 // ---------------------------------------------------------------------------
+// Barrier over a subset of the CTA's warps (named barrier `id`, `count`
+// threads, a multiple of 32).
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -32,8 +32,12 @@ namespace tj {
 // Epilogue warps per CTA: 8 for the residual epilogue (each thread keeps the
 // prefetched residual of its row in registers), 16 for the fp16 epilogues
 // (GELU is ALU-heavy; more warps hide its latency).
-__host__ __device__ constexpr int epi_warps_for(int epi) { return epi == 1 ? 8 : 16; }
-__host__ __device__ constexpr int gemm_threads_for(int epi) { return 64 + 32 * epi_warps_for(epi); }
+__host__ __device__ constexpr int epi_warps_for(int bn, int epi) {
+  return bn < 256 ? 8 : (epi == 1 ? 8 : 16);
+}
+__host__ __device__ constexpr int gemm_threads_for(int bn, int epi) {
+  return 64 + 32 * epi_warps_for(bn, epi);
+}
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kHeadPad = 64;  // head-major row length (halves) of the QKV output
@@ -52,7 +56,7 @@ struct GemmKernelParams {
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -75,12 +79,12 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(gemm_threads_for(EPI), 1)
+__global__ void __launch_bounds__(gemm_threads_for(BN, EPI), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmKernelParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
-  constexpr int kEpiWarps = epi_warps_for(EPI);
+  constexpr int kEpiWarps = epi_warps_for(BN, EPI);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
@@ -236,12 +240,19 @@ __global__ void __launch_bounds__(gemm_threads_for(EPI), 1)
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, 130 + EPI)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      // fp16 epilogues load two TMEM chunks per wait; the residual one keeps
+      // 128 registers of prefetched residual and loads one.
+      constexpr int kPerWait = (EPI == kEpiResidualF32 || kChunks < 2) ? 1 : 2;
+      uint32_t rbuf[kPerWait][32];
 #pragma unroll
       for (int cc = 0; cc < kChunks; ++cc) {
         const int c = slice * kChunks + cc;
-        uint32_t r[32];
-        tmem_ld32(t_row + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
+        if (cc % kPerWait == 0) {
+#pragma unroll
+          for (int u = 0; u < kPerWait; ++u) tmem_ld32(t_row + (uint32_t)((c + u) * 32), rbuf[u]);
+          tmem_ld_wait();
+        }
+        const uint32_t (&r)[32] = rbuf[cc % kPerWait];
         const int nc = n0 + c * 32;
         if (!row_ok || nc >= p.N) continue;
 #pragma unroll
@@ -395,11 +406,24 @@ static int launch_gemm_t(const GemmArgs& a, const GemmKernelParams& kp, cudaStre
   const int max_tiles = ((a.rows_max + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
   const int grid = max_tiles < num_sms ? max_tiles : num_sms;
   if (grid <= 0) return TJ_OK;
-  cudaError_t e = launch_pdl(gemm_tcgen05_kernel<BN, EPI>, dim3(grid), dim3(gemm_threads_for(EPI)),
+  cudaError_t e = launch_pdl(gemm_tcgen05_kernel<BN, EPI>, dim3(grid), dim3(gemm_threads_for(BN, EPI)),
                              Cfg::kSmemBytes, stream, ta, tb, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
   return TJ_OK;
+}
+
+// 256-column tiles keep the operand traffic per FLOP low; when they would give
+// fewer tiles than SMs (small batches), 64-column tiles spread the work (and
+// the per-tile epilogue) over four times as many SMs.
+template <int EPI>
+static int launch_gemm_bn(const GemmArgs& a, const GemmKernelParams& kp, cudaStream_t stream) {
+  int num_sms = 0;
+  int rc = ensure_device_props(&num_sms);
+  if (rc) return rc;
+  const long long tiles256 = (long long)((a.rows_max + kBM - 1) / kBM) * ((a.N + 255) / 256);
+  if (tiles256 < num_sms) return launch_gemm_t<64, EPI>(a, kp, stream);
+  return launch_gemm_t<256, EPI>(a, kp, stream);
 }
 
 int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
@@ -433,16 +457,16 @@ int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
                          "gemm_qkv_headmajor: N=%d must be 3*H*dh with dh <= %d (H=%d dh=%d)",
                          a.N, kHeadPad, a.heads, a.head_dim);
       kp.d_model = a.heads * a.head_dim;
-      return launch_gemm_t<256, kEpiQkvHeadMajor>(a, kp, stream);
+      return launch_gemm_bn<kEpiQkvHeadMajor>(a, kp, stream);
     case kEpiResidualF32:
       if (!a.resid || (reinterpret_cast<uintptr_t>(a.resid) & 15u) || a.ld_resid % 4 != 0 ||
           a.ld_out % 4 != 0)
         return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_residual_f32: residual must be 16-byte aligned");
-      return launch_gemm_t<256, kEpiResidualF32>(a, kp, stream);
+      return launch_gemm_bn<kEpiResidualF32>(a, kp, stream);
     case kEpiGeluF16:
       if (a.ld_out % 8 != 0)
         return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_gelu_f16: ld_out must be a multiple of 8");
-      return launch_gemm_t<256, kEpiGeluF16>(a, kp, stream);
+      return launch_gemm_bn<kEpiGeluF16>(a, kp, stream);
     default:
       return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epilogue);
   }

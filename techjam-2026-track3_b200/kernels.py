@@ -36,6 +36,14 @@ def _require(t: torch.Tensor, name: str, dtype: torch.dtype, device: torch.devic
         raise ValueError(f"{name} must be contiguous")
 
 
+def _require_out(out: torch.Tensor, name: str, shape, dtype: torch.dtype, device: torch.device) -> None:
+    """A caller-provided output must be exactly the buffer the kernel writes:
+    the C ABI takes raw pointers and cannot check sizes itself."""
+    _require(out, name, dtype, device)
+    if tuple(out.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(out.shape)}")
+
+
 def token_plan(mask: Optional[torch.Tensor], batch: int, seq_len: int, device) -> torch.Tensor:
     lib = _lib.load()
     n = lib.tj_token_plan_ints(batch, seq_len)
@@ -71,6 +79,9 @@ def ln_cast_f16(x, gamma, beta, eps=1e-5, row_map=None, row_count=None, out=None
     rows = x.numel() // D if row_map is None else row_map.numel()
     if out is None:
         out = torch.empty(rows, D, dtype=torch.float16, device=dev)
+    if out.dim() != 2 or out.shape[1] != D or out.shape[0] < rows:
+        raise ValueError(f"out must be [>= {rows}, {D}], got {tuple(out.shape)}")
+    _require(out, "out", torch.float16, dev)
     lib = _lib.load()
     rc = lib.tj_ln_cast_f16(
         x.data_ptr(), _ptr(row_map), _ptr(row_count), rows, D, gamma.data_ptr(), beta.data_ptr(),
@@ -88,6 +99,7 @@ def ln_final_mask(x, gamma, beta, eps=1e-5, inv_map=None, rows=None, out=None):
         rows = x.numel() // D if inv_map is None else inv_map.numel()
     if out is None:
         out = torch.empty(rows, D, dtype=torch.float32, device=dev)
+    _require_out(out, "out", (rows, D), torch.float32, dev)
     lib = _lib.load()
     rc = lib.tj_ln_final_mask(
         x.data_ptr(), _ptr(inv_map), rows, D, gamma.data_ptr(), beta.data_ptr(), float(eps),
@@ -108,6 +120,7 @@ def gemm_qkv_headmajor(a16, w_qkv16, b_qkv, num_heads, row_count=None, out=None)
     if out is None:
         # head-major, each head zero-padded to 64 halves
         out = torch.empty(3, num_heads, rows, 64, dtype=torch.float16, device=dev)
+    _require_out(out, "out", (3, num_heads, rows, 64), torch.float16, dev)
     lib = _lib.load()
     rc = lib.tj_gemm_qkv_headmajor(
         a16.data_ptr(), w_qkv16.data_ptr(), b_qkv.data_ptr(), _ptr(row_count), rows, D, num_heads,
@@ -129,6 +142,13 @@ def gemm_bias_residual_f32(a16, w16, bias, resid, resid_map=None, row_count=None
         raise ValueError("w16 inner dimension does not match a16")
     if out is None:
         out = torch.empty(rows, N, dtype=torch.float32, device=dev)
+    if out.dim() != 2 or out.shape[1] != N or out.shape[0] < (rows if row_count is None else 1):
+        raise ValueError(f"out must be [rows, {N}], got {tuple(out.shape)}")
+    _require(out, "out", torch.float32, dev)
+    if resid.dim() != 2 or resid.shape[1] != N:
+        raise ValueError(f"resid must be [rows, {N}], got {tuple(resid.shape)}")
+    if resid_map is None and row_count is None and resid.shape[0] < rows:
+        raise ValueError("resid has fewer rows than a16")
     lib = _lib.load()
     rc = lib.tj_gemm_bias_residual_f32(
         a16.data_ptr(), w16.data_ptr(), bias.data_ptr(), resid.data_ptr(), _ptr(resid_map),
@@ -149,6 +169,7 @@ def gemm_bias_gelu_f16(a16, w16, bias, row_count=None, out=None):
         raise ValueError("w16 inner dimension does not match a16")
     if out is None:
         out = torch.empty(rows, N, dtype=torch.float16, device=dev)
+    _require_out(out, "out", (rows, N), torch.float16, dev)
     lib = _lib.load()
     rc = lib.tj_gemm_bias_gelu_f16(
         a16.data_ptr(), w16.data_ptr(), bias.data_ptr(), _ptr(row_count), rows, N, K,
@@ -174,9 +195,16 @@ def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causa
     if k.stride() != v.stride() or k.stride(-1) != 1 or k.stride(-2) != 64:
         raise ValueError("k and v must share strides with contiguous [rows, 64] slabs")
     dh = head_dim
+    if not 1 <= dh <= 64:
+        raise ValueError(f"head_dim must be in 1..64, got {dh}")
     B = q_cu.numel() - 1
     if out is None:
         out = torch.empty(q.shape[1], H * dh, dtype=torch.float16, device=dev)
+    _require_out(out, "out", (q.shape[1], H * dh), torch.float16, dev)
+    for name, t in (("q_cu", q_cu), ("kv_off", kv_off), ("kv_len", kv_len)):
+        _require(t, name, torch.int32, dev)
+    if kv_off.numel() != B * G or kv_len.numel() != B * G:
+        raise ValueError(f"kv_off/kv_len must hold {B}x{G} entries")
     lib = _lib.load()
     rc = lib.tj_flash_attn_fwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), H, dh, q.shape[1], kv_rows, k.stride(1),

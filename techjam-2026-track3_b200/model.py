@@ -18,6 +18,7 @@ tensor, a non-fp32 input, training mode or a missing library raises.
 from __future__ import annotations
 
 import ctypes
+from collections import OrderedDict
 from dataclasses import dataclass
 from typing import Any, Optional
 
@@ -111,6 +112,8 @@ class UserOptimizedTransformer(nn.Module):
         self._large_sequence_compile_fullgraph = False
         self.__dict__["_workspace"] = None
         self.__dict__["_layer_structs"] = None
+        self.__dict__["_graphs"] = OrderedDict()
+        self.use_cuda_graphs = True
         self._refresh_mixed_weights()
 
     # ---- weight caches ------------------------------------------------------
@@ -130,6 +133,7 @@ class UserOptimizedTransformer(nn.Module):
             layer._ffn_in_weight_mixed = self._cast_cache(layer.ffn_in.weight)
             layer._ffn_out_weight_mixed = self._cast_cache(layer.ffn_out.weight)
         self.__dict__["_layer_structs"] = None
+        self._drop_graphs()
 
     def load_state_dict(self, state_dict, *args, **kwargs):
         result = super().load_state_dict(state_dict, *args, **kwargs)
@@ -215,6 +219,7 @@ class UserOptimizedTransformer(nn.Module):
             raise ValueError("invalid encoder shape")
         ws = self.__dict__.get("_workspace")
         if ws is None or ws.device != device or ws.numel() < need:
+            self._drop_graphs()  # captured graphs point at the old workspace
             ws = torch.empty(need, dtype=torch.uint8, device=device)
             self.__dict__["_workspace"] = ws
         return ws
@@ -245,8 +250,8 @@ class UserOptimizedTransformer(nn.Module):
                 mask = mask.view(torch.uint8)
         return x.contiguous(), mask
 
-    def _forward_impl(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
-        x, mask = self._check_inputs(x, valid_token_mask)
+    def _launch(self, x: torch.Tensor, mask: Optional[torch.Tensor], out: torch.Tensor) -> None:
+        """One tj_encoder_forward call on the current stream."""
         B, S, D = x.shape
         cfg = self.config
         desc = _lib.EncoderDesc(B, S, D, cfg.num_heads, cfg.ffn_dim, len(self.layers), 1 if cfg.causal else 0,
@@ -254,7 +259,6 @@ class UserOptimizedTransformer(nn.Module):
         lib = _lib.load()
         ws = self._workspace_for(desc, x.device)
         weights = self._layer_weights(x.device)
-        out = torch.empty_like(x)
         stream = torch.cuda.current_stream(x.device).cuda_stream
         rc = lib.tj_encoder_forward(
             ctypes.byref(desc), weights, self.final_norm.weight.data_ptr(), self.final_norm.bias.data_ptr(),
@@ -262,6 +266,65 @@ class UserOptimizedTransformer(nn.Module):
             ws.numel(), ctypes.c_void_p(stream),
         )
         _lib.check(rc, "encoder_forward")
+
+    # ---- CUDA graphs for small problems -------------------------------------
+    # Each kernel launch costs a few microseconds of host work (argument checks,
+    # tensor-map encoding, the launch itself).  A small problem's whole forward
+    # takes about that long per kernel on the GPU, so the GPU would wait for
+    # the host.  For inputs up to _GRAPH_MAX_INPUT_BYTES the forward of each
+    # input shape is captured once into a CUDA graph over static input, mask
+    # and output buffers; a call copies its input in, replays the graph and
+    # returns a copy of the output (so later calls never alias it).
+    _GRAPH_MAX_INPUT_BYTES = 32 << 20
+    _GRAPH_CACHE_SIZE = 8
+
+    def _drop_graphs(self) -> None:
+        graphs = self.__dict__.get("_graphs")
+        if graphs:
+            graphs.clear()
+
+    def _graph_forward(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+        dev = x.device
+        stream = torch.cuda.current_stream(dev)
+        key = (dev, tuple(x.shape), mask is None, stream.cuda_stream)
+        graphs = self.__dict__["_graphs"]
+        entry = graphs.get(key)
+        if entry is None:
+            sx = torch.empty_like(x)
+            sm = None if mask is None else torch.empty_like(mask)
+            so = torch.empty_like(x)
+            sx.copy_(x)
+            if sm is not None:
+                sm.copy_(mask)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):  # warm-up: kernel attributes, workspace
+                self._launch(sx, sm, so)
+            stream.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._launch(sx, sm, so)
+            entry = (graph, sx, sm, so)
+            graphs[key] = entry
+            while len(graphs) > self._GRAPH_CACHE_SIZE:
+                graphs.popitem(last=False)
+        else:
+            graphs.move_to_end(key)
+        graph, sx, sm, so = entry
+        sx.copy_(x)
+        if sm is not None:
+            sm.copy_(mask)
+        graph.replay()
+        return so.clone()
+
+    def _forward_impl(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
+        x, mask = self._check_inputs(x, valid_token_mask)
+        if (self.use_cuda_graphs and x.numel() * 4 <= self._GRAPH_MAX_INPUT_BYTES
+                and not _lib.sync_check_enabled()
+                and not torch.cuda.is_current_stream_capturing()):
+            return self._graph_forward(x, mask)
+        out = torch.empty_like(x)
+        self._launch(x, mask, out)
         return out
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -118,7 +118,8 @@ def test_gemm_qkv_headmajor(cuda_pkg, rows, count, D, H):
         assert torch.isnan(out[:, :, count:].float()).all(), "rows past the count must not be written"
 
 
-@pytest.mark.parametrize("rows,count,N,K", [(256, 200, 1024, 1024), (1000, 1000, 768, 3072), (640, 513, 256, 256)])
+@pytest.mark.parametrize("rows,count,N,K",
+                         [(256, 200, 1024, 1024), (1000, 1000, 768, 3072), (640, 513, 256, 256), (40000, 39000, 1024, 1024)])
 def test_gemm_bias_residual_f32(cuda_pkg, rows, count, N, K):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(rows + N + K)
@@ -133,7 +134,7 @@ def test_gemm_bias_residual_f32(cuda_pkg, rows, count, N, K):
     torch.testing.assert_close(out[:count], ref[:count], rtol=1e-4, atol=1e-3)
 
 
-@pytest.mark.parametrize("rows,N,K", [(512, 4096, 1024), (333, 3072, 768), (128, 1024, 256)])
+@pytest.mark.parametrize("rows,N,K", [(512, 4096, 1024), (333, 3072, 768), (128, 1024, 256), (100, 136, 96)])
 def test_gemm_bias_gelu_f16(cuda_pkg, rows, N, K):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(rows + N)

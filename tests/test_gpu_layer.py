@@ -155,3 +155,39 @@ def test_rejects_unsupported_inputs(cuda_pkg):
     model.train()
     with pytest.raises(RuntimeError):
         model(torch.zeros(1, 128, 256, device=DEV))
+
+
+def test_cuda_graph_replay_matches_eager(cuda_pkg):
+    """Small problems replay a captured CUDA graph; results must equal the eager
+    launches bit for bit, follow in-place updates of the input buffer, and pick
+    up reloaded weights."""
+    prev = cuda_pkg._lib.set_sync_check(False)
+    try:
+        cfg = oracle.TransformerConfig(4, 128, 128, 4, 128, 2, True)
+        sd = oracle.make_state_dict(cfg, seed=3)
+        x, mask = oracle.generate_random_case(cfg, seed=3, padding_ratio=0.3)
+        model = _model(cuda_pkg, cfg, sd)
+        xd, md = x.to(DEV), mask.to(DEV)
+        with torch.inference_mode():
+            model.use_cuda_graphs = False
+            eager = model(xd, md)
+            model.use_cuda_graphs = True
+            g1 = model(xd, md)
+            g2 = model(xd, md)
+            assert torch.equal(eager, g1) and torch.equal(eager, g2)
+            assert len(model._graphs) == 1
+            assert g1.data_ptr() != g2.data_ptr()  # outputs never alias
+            xd = xd * 0.5  # a new input buffer of the same shape reuses the graph
+            model.use_cuda_graphs = False
+            eager2 = model(xd, md)
+            model.use_cuda_graphs = True
+            assert torch.equal(model(xd, md), eager2)
+            assert len(model._graphs) == 1
+            sd2 = oracle.make_state_dict(cfg, seed=4)
+            model.load_state_dict(sd2, strict=True)
+            assert len(model._graphs) == 0
+            g3 = model(xd, md)
+        torch.cuda.synchronize()
+        _gate(oracle.encoder_forward(sd2, cfg, x * 0.5, mask), g3, "graph after reload")
+    finally:
+        cuda_pkg._lib.set_sync_check(prev)
