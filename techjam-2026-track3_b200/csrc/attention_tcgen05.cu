@@ -564,8 +564,14 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
     rc = make_tmap_f16(&tv, a.v, 4, d, s, bx);
     if (rc) return rc;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
+  {
+    int num_sms = 0;
+    int rc = ensure_device_props(&num_sms);
+    if (rc) return rc;
+  }
+  static bool attr_set[64] = {};
+  const int dev = device_index();
+  if (!attr_set[dev]) {
     cudaFuncAttributes fa;
     cudaError_t e0 = cudaFuncGetAttributes(&fa, attention_tcgen05_kernel);
     if (e0 != cudaSuccess)
@@ -579,7 +585,7 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem);
     if (e != cudaSuccess)
       return set_error(TJ_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
-    attr_set = true;
+    attr_set[dev] = true;
   }
   AttnKernelParams kp{};
   kp.H = a.H;

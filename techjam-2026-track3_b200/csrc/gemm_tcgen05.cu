@@ -78,6 +78,115 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// Epilogue of one accumulator tile for one epilogue warp: prefetch the
+// residual (before waiting, so its latency hides behind the main loop), wait
+// for the accumulator, then bias + fused op + store for the warp's rows
+// (TMEM lane quarter) and column slice.  Returns false if the CTA aborts.
+template <int BN, int EPI, int kEpiWarps>
+__device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_t tmem_acc, int m0,
+                                              int n0, int rows, int quarter, int slice, uint32_t lane,
+                                              uint32_t tfull_bar, uint32_t tfull_parity,
+                                              volatile int* abort_flag) {
+  constexpr int kSlices = kEpiWarps / 4;
+  constexpr int kChunks = BN / 32 / kSlices;
+  const int row_in_tile = quarter * 32 + (int)lane;
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < rows;
+      // Residual rows are fetched before waiting for the accumulator, so their
+      // DRAM latency hides behind the tile's main loop.
+      float4 res[EPI == kEpiResidualF32 ? kChunks : 1][8];
+      if (EPI == kEpiResidualF32) {
+        const int64_t resid_row = row_ok ? (p.resid_map ? (int64_t)p.resid_map[row] : (int64_t)row) : 0;
+#pragma unroll
+        for (int cc = 0; cc < kChunks; ++cc) {
+          const int nc = n0 + (slice * kChunks + cc) * 32;
+          const float4* rs = reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + nc);
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            res[cc][g] = (row_ok && nc + 4 * g < p.N) ? __ldg(rs + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      if (!mbar_wait(tfull_bar, tfull_parity, abort_flag, 130 + EPI)) return false;
+      tc_fence_after();
+      const uint32_t t_row = tmem_acc + ((uint32_t)(quarter * 32) << 16);
+      // fp16 epilogues load two TMEM chunks per wait; the residual one keeps
+      // 128 registers of prefetched residual and loads one.
+      constexpr int kPerWait = (EPI == kEpiResidualF32 || kChunks < 2) ? 1 : 2;
+      uint32_t rbuf[kPerWait][32];
+#pragma unroll
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int c = slice * kChunks + cc;
+        if (cc % kPerWait == 0) {
+#pragma unroll
+          for (int u = 0; u < kPerWait; ++u) tmem_ld32(t_row + (uint32_t)((c + u) * 32), rbuf[u]);
+          tmem_ld_wait();
+        }
+        const uint32_t (&r)[32] = rbuf[cc % kPerWait];
+        const int nc = n0 + c * 32;
+        if (!row_ok || nc >= p.N) continue;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int n = nc + 8 * g;
+          if (n >= p.N) break;
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + n) + 1);
+          float w[8] = {__uint_as_float(r[8 * g + 0]) + b0.x, __uint_as_float(r[8 * g + 1]) + b0.y,
+                        __uint_as_float(r[8 * g + 2]) + b0.z, __uint_as_float(r[8 * g + 3]) + b0.w,
+                        __uint_as_float(r[8 * g + 4]) + b1.x, __uint_as_float(r[8 * g + 5]) + b1.y,
+                        __uint_as_float(r[8 * g + 6]) + b1.z, __uint_as_float(r[8 * g + 7]) + b1.w};
+          if (EPI == kEpiQkvHeadMajor) {
+            // Head-major rows are kHeadPad (64) halves; a head dim below 64 is
+            // stored zero-padded, so attention always sees 64-wide rows.
+            __half* qkv = static_cast<__half*>(p.out);
+            if ((p.head_dim & 7) == 0) {
+              const int which = n / p.d_model;
+              const int rem = n - which * p.d_model;
+              const int h = rem / p.head_dim;
+              const int d = rem - h * p.head_dim;
+              __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
+              uint4 o;
+              o.x = pack_half2(w[0], w[1]);
+              o.y = pack_half2(w[2], w[3]);
+              o.z = pack_half2(w[4], w[5]);
+              o.w = pack_half2(w[6], w[7]);
+              *reinterpret_cast<uint4*>(rowp + d) = o;
+              if (d + 8 == p.head_dim)
+                for (int z = p.head_dim; z < kHeadPad; z += 8)
+                  *reinterpret_cast<uint4*>(rowp + z) = make_uint4(0u, 0u, 0u, 0u);
+            } else {
+              for (int e = 0; e < 8; ++e) {
+                const int ne = n + e;
+                const int which = ne / p.d_model;
+                const int rem = ne - which * p.d_model;
+                const int h = rem / p.head_dim;
+                const int d = rem - h * p.head_dim;
+                __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
+                rowp[d] = __float2half_rn(w[e]);
+                if (d + 1 == p.head_dim)
+                  for (int z = p.head_dim; z < kHeadPad; ++z) rowp[z] = __float2half_rn(0.f);
+              }
+            }
+          } else if (EPI == kEpiGeluF16) {
+            __half* dst = static_cast<__half*>(p.out) + (int64_t)row * p.ld_out + n;
+            uint4 o;
+            o.x = pack_half2(gelu_erf(w[0]), gelu_erf(w[1]));
+            o.y = pack_half2(gelu_erf(w[2]), gelu_erf(w[3]));
+            o.z = pack_half2(gelu_erf(w[4]), gelu_erf(w[5]));
+            o.w = pack_half2(gelu_erf(w[6]), gelu_erf(w[7]));
+            *reinterpret_cast<uint4*>(dst) = o;
+          } else {
+            const float4 r0 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g];
+            const float4 r1 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g + 1];
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                    (int64_t)row * p.ld_out + n);
+            dst[0] = make_float4(w[0] + r0.x, w[1] + r0.y, w[2] + r0.z, w[3] + r0.w);
+            dst[1] = make_float4(w[4] + r1.x, w[5] + r1.y, w[6] + r1.z, w[7] + r1.w);
+          }
+        }
+      }
+  return true;
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(gemm_threads_for(BN, EPI), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -210,111 +319,17 @@ __global__ void __launch_bounds__(gemm_threads_for(BN, EPI), 1)
     }
   } else {
     // Epilogue warps: TMEM lane quarter = warp % 4; the kEpiWarps/4 warps of a
-    // quarter split the tile's columns into slices of kChunks x 32.
-    constexpr int kSlices = kEpiWarps / 4;
-    constexpr int kChunks = BN / 32 / kSlices;
+    // quarter split the tile's columns into slices.
     const int quarter = warp & 3;
     const int slice = (warp - 2) >> 2;
-    const int row_in_tile = quarter * 32 + (int)lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
       const int m0 = (t / n_tiles) * kBM;
       const int n0 = (t % n_tiles) * BN;
-      const int row = m0 + row_in_tile;
-      const bool row_ok = row < rows;
-      // Residual rows are fetched before waiting for the accumulator, so their
-      // DRAM latency hides behind the tile's main loop.
-      float4 res[EPI == kEpiResidualF32 ? kChunks : 1][8];
-      if (EPI == kEpiResidualF32) {
-        const int64_t resid_row = row_ok ? (p.resid_map ? (int64_t)p.resid_map[row] : (int64_t)row) : 0;
-#pragma unroll
-        for (int cc = 0; cc < kChunks; ++cc) {
-          const int nc = n0 + (slice * kChunks + cc) * 32;
-          const float4* rs = reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + nc);
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            res[cc][g] = (row_ok && nc + 4 * g < p.N) ? __ldg(rs + g) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, 130 + EPI)) break;
-      tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      // fp16 epilogues load two TMEM chunks per wait; the residual one keeps
-      // 128 registers of prefetched residual and loads one.
-      constexpr int kPerWait = (EPI == kEpiResidualF32 || kChunks < 2) ? 1 : 2;
-      uint32_t rbuf[kPerWait][32];
-#pragma unroll
-      for (int cc = 0; cc < kChunks; ++cc) {
-        const int c = slice * kChunks + cc;
-        if (cc % kPerWait == 0) {
-#pragma unroll
-          for (int u = 0; u < kPerWait; ++u) tmem_ld32(t_row + (uint32_t)((c + u) * 32), rbuf[u]);
-          tmem_ld_wait();
-        }
-        const uint32_t (&r)[32] = rbuf[cc % kPerWait];
-        const int nc = n0 + c * 32;
-        if (!row_ok || nc >= p.N) continue;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int n = nc + 8 * g;
-          if (n >= p.N) break;
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + n) + 1);
-          float w[8] = {__uint_as_float(r[8 * g + 0]) + b0.x, __uint_as_float(r[8 * g + 1]) + b0.y,
-                        __uint_as_float(r[8 * g + 2]) + b0.z, __uint_as_float(r[8 * g + 3]) + b0.w,
-                        __uint_as_float(r[8 * g + 4]) + b1.x, __uint_as_float(r[8 * g + 5]) + b1.y,
-                        __uint_as_float(r[8 * g + 6]) + b1.z, __uint_as_float(r[8 * g + 7]) + b1.w};
-          if (EPI == kEpiQkvHeadMajor) {
-            // Head-major rows are kHeadPad (64) halves; a head dim below 64 is
-            // stored zero-padded, so attention always sees 64-wide rows.
-            __half* qkv = static_cast<__half*>(p.out);
-            if ((p.head_dim & 7) == 0) {
-              const int which = n / p.d_model;
-              const int rem = n - which * p.d_model;
-              const int h = rem / p.head_dim;
-              const int d = rem - h * p.head_dim;
-              __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
-              uint4 o;
-              o.x = pack_half2(w[0], w[1]);
-              o.y = pack_half2(w[2], w[3]);
-              o.z = pack_half2(w[4], w[5]);
-              o.w = pack_half2(w[6], w[7]);
-              *reinterpret_cast<uint4*>(rowp + d) = o;
-              if (d + 8 == p.head_dim)
-                for (int z = p.head_dim; z < kHeadPad; z += 8)
-                  *reinterpret_cast<uint4*>(rowp + z) = make_uint4(0u, 0u, 0u, 0u);
-            } else {
-              for (int e = 0; e < 8; ++e) {
-                const int ne = n + e;
-                const int which = ne / p.d_model;
-                const int rem = ne - which * p.d_model;
-                const int h = rem / p.head_dim;
-                const int d = rem - h * p.head_dim;
-                __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
-                rowp[d] = __float2half_rn(w[e]);
-                if (d + 1 == p.head_dim)
-                  for (int z = p.head_dim; z < kHeadPad; ++z) rowp[z] = __float2half_rn(0.f);
-              }
-            }
-          } else if (EPI == kEpiGeluF16) {
-            __half* dst = static_cast<__half*>(p.out) + (int64_t)row * p.ld_out + n;
-            uint4 o;
-            o.x = pack_half2(gelu_erf(w[0]), gelu_erf(w[1]));
-            o.y = pack_half2(gelu_erf(w[2]), gelu_erf(w[3]));
-            o.z = pack_half2(gelu_erf(w[4]), gelu_erf(w[5]));
-            o.w = pack_half2(gelu_erf(w[6]), gelu_erf(w[7]));
-            *reinterpret_cast<uint4*>(dst) = o;
-          } else {
-            const float4 r0 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g];
-            const float4 r1 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g + 1];
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
-                                                    (int64_t)row * p.ld_out + n);
-            dst[0] = make_float4(w[0] + r0.x, w[1] + r0.y, w[2] + r0.z, w[3] + r0.w);
-            dst[1] = make_float4(w[4] + r1.x, w[5] + r1.y, w[6] + r1.z, w[7] + r1.w);
-          }
-        }
-      }
+      if (!epilogue_tile<BN, EPI, kEpiWarps>(p, tmem_base + (uint32_t)(acc * BN), m0, n0, rows, quarter,
+                                             slice, lane, tfull_bar(acc), acc_phase, abort_flag))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -331,6 +346,204 @@ __global__ void __launch_bounds__(gemm_threads_for(BN, EPI), 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant for large problems: a cluster of two CTAs (on two SMs)
+// computes one 256 x 256 tile with tcgen05.mma.cta_group::2 (M=256, N=256).
+// CTA r loads rows m0+128r.. of A and rows n0+128r.. of W (32 KB per K block
+// instead of 48 KB for a 128 x 256 tile on one SM), which leaves room for six
+// pipeline stages; its TMEM holds rows m0+128r.. of the accumulator for all
+// 256 columns, so the epilogue is the one-CTA epilogue at BN=256.
+//   - Both CTAs' TMA loads complete on the leader's (rank 0) full barrier;
+//     the leader's producer expects the bytes of both.
+//   - The leader's MMA lane issues the pair MMAs and commits, once to its own
+//     barrier and once to the peer's, for the stage-empty and
+//     accumulator-full events (no multicast).
+//   - Each CTA's epilogue warps arrive on the leader's accumulator-empty
+//     barrier (count 2 x epilogue warps).
+// Every wait is bounded as in the one-CTA kernel; both CTAs meet at a cluster
+// barrier before TMEM is freed, so neither leaves while the other can still
+// touch its shared memory.
+// ---------------------------------------------------------------------------
+struct PairCfg {
+  static constexpr int kBN = 256;
+  static constexpr int kStages = 6;
+  static constexpr uint32_t kABytes = kBM * kBK * 2;            // this CTA's 128 rows of A
+  static constexpr uint32_t kBBytes = (kBN / 2) * kBK * 2;      // this CTA's 128 rows of W
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = 2 * kBN;
+  static constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256, EPI), 1)
+    gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                             const __grid_constant__ CUtensorMap tmB, const GemmKernelParams p) {
+  using Cfg = PairCfg;
+  constexpr int S = Cfg::kStages;
+  constexpr int BN = Cfg::kBN;
+  constexpr int kEpiWarps = epi_warps_for(BN, EPI);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+  // bars: full[S] (leader's used), empty[S], tfull[2], tempty[2] (leader's used), final
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_idx();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + S + s); };
+  auto tfull_bar = [&](int a) { return smem_u32(bars + 2 * S + a); };
+  auto tempty_bar = [&](int a) { return smem_u32(bars + 2 * S + 2 + a); };
+  const uint32_t final_bar = smem_u32(bars + 2 * S + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 2 * kEpiWarps);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = device_failed() ? 1 : 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+
+  const int rows = p.row_count ? min(p.rows_max, *p.row_count) : p.rows_max;
+  const int m_tiles = (rows + 2 * kBM - 1) / (2 * kBM);
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int total_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+  const int cluster_id = (int)(blockIdx.x >> 1);
+  const int num_clusters = (int)(gridDim.x >> 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_parity[S];
+      for (int s = 0; s < S; ++s) last_parity[s] = -1;
+      for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters) {
+        const int m0 = (t / n_tiles) * (2 * kBM) + (int)rank * kBM;
+        const int n0 = (t % n_tiles) * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, 140 + EPI)) break;
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * Cfg::kStageBytes);
+          const uint32_t leader_full = mapa_shared(full_bar(stage), 0);
+          tma_load_2d_pair(smem_u32(sA + stage * Cfg::kABytes), &tmA, leader_full, kb * kBK, m0);
+          tma_load_2d_pair(smem_u32(sB + stage * Cfg::kBBytes), &tmB, leader_full, kb * kBK, n0);
+          last_parity[stage] = (int)phase;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // The leader's full barriers count both CTAs' loads: once they have
+      // completed, nothing either CTA issued is still landing.
+      if (leader)
+        for (int s = 0; s < S; ++s)
+          if (last_parity[s] >= 0) drain_wait(full_bar(s), (uint32_t)last_parity[s]);
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(2 * kBM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued = false;
+      for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters) {
+        if (!mbar_wait<true>(tempty_bar(acc), acc_phase ^ 1, abort_flag, 150 + EPI)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, 160 + EPI)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a_desc = sw128_desc(smem_u32(sA + stage * Cfg::kABytes), 16, 1024);
+          const uint64_t b_desc = sw128_desc(smem_u32(sB + stage * Cfg::kBBytes), 16, 1024);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_f16_ss_pair(d_tmem, a_desc + (uint64_t)(2 * k), b_desc + (uint64_t)(2 * k), idesc,
+                            (kb | k) != 0 ? 1u : 0u);
+          issued = true;
+          mma_commit_pair(empty_bar(stage));
+          mma_commit_pair(mapa_shared(empty_bar(stage), 1));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(tfull_bar(acc));
+        mma_commit_pair(mapa_shared(tfull_bar(acc), 1));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (issued) {
+        mma_commit_pair(final_bar);
+        drain_wait(final_bar, 0);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int slice = (warp - 2) >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters) {
+      const int m0 = (t / n_tiles) * (2 * kBM) + (int)rank * kBM;
+      const int n0 = (t % n_tiles) * BN;
+      if (!epilogue_tile<BN, EPI, kEpiWarps>(p, tmem_base + (uint32_t)(acc * BN), m0, n0, rows, quarter,
+                                             slice, lane, tfull_bar(acc), acc_phase, abort_flag))
+        break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  __syncwarp();
+  pdl_trigger();
+  tc_fence_before();
+  cluster_sync();  // the peer no longer reads this CTA's shared memory or barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -391,18 +604,19 @@ static int launch_gemm_t(const GemmArgs& a, const GemmKernelParams& kp, cudaStre
   rc = make_tmap_f16(&tb, a.w16, 2, db, sb, bb);
   if (rc) return rc;
 
-  static bool attr_set = false;
-  if (!attr_set) {
+  int num_sms = 0;
+  rc = ensure_device_props(&num_sms);
+  if (rc) return rc;
+  static bool attr_set[64] = {};
+  const int dev = device_index();
+  if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)Cfg::kSmemBytes);
     if (e != cudaSuccess)
       return set_error(TJ_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
-    attr_set = true;
+    attr_set[dev] = true;
   }
-  int num_sms = 0;
-  rc = ensure_device_props(&num_sms);
-  if (rc) return rc;
   const int max_tiles = ((a.rows_max + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
   const int grid = max_tiles < num_sms ? max_tiles : num_sms;
   if (grid <= 0) return TJ_OK;
@@ -410,6 +624,66 @@ static int launch_gemm_t(const GemmArgs& a, const GemmKernelParams& kp, cudaStre
                              Cfg::kSmemBytes, stream, ta, tb, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+  return TJ_OK;
+}
+
+// Co-resident CTA-pair clusters of the pair kernel (0 if it cannot launch).
+template <int EPI>
+static int pair_clusters() {
+  int num_sms = 0;
+  if (ensure_device_props(&num_sms)) return 0;
+  static int cache[64];
+  static bool known[64] = {};
+  const int dev = device_index();
+  int& cached = cache[dev];
+  if (known[dev]) return cached;
+  known[dev] = true;
+  cached = 0;
+  if (cudaFuncSetAttribute(gemm_tcgen05_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)PairCfg::kSmemBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return cached;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms & ~1);
+  cfg.blockDim = dim3(gemm_threads_for(256, EPI));
+  cfg.dynamicSmemBytes = PairCfg::kSmemBytes;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tcgen05_pair_kernel<EPI>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cached = n;
+  return cached;
+}
+
+static bool pair_gemm_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("TJ_GEMM_PAIR");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
+}
+
+template <int EPI>
+static int launch_gemm_pair(const GemmArgs& a, const GemmKernelParams& kp, int clusters,
+                            cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  uint64_t da[2] = {(uint64_t)a.K, (uint64_t)a.rows_max};
+  uint64_t sa[1] = {(uint64_t)a.K};
+  uint32_t ba[2] = {kBK, kBM};
+  int rc = make_tmap_f16(&ta, a.a16, 2, da, sa, ba);
+  if (rc) return rc;
+  uint64_t db[2] = {(uint64_t)a.K, (uint64_t)a.N};
+  uint64_t sb[1] = {(uint64_t)a.K};
+  uint32_t bb[2] = {kBK, (uint32_t)(PairCfg::kBN / 2)};
+  rc = make_tmap_f16(&tb, a.w16, 2, db, sb, bb);
+  if (rc) return rc;
+  cudaError_t e = launch_pdl(gemm_tcgen05_pair_kernel<EPI>, dim3(2 * clusters),
+                             dim3(gemm_threads_for(256, EPI)), PairCfg::kSmemBytes, stream, ta, tb, kp);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "gemm pair launch: %s", cudaGetErrorString(e));
   return TJ_OK;
 }
 
@@ -423,6 +697,11 @@ static int launch_gemm_bn(const GemmArgs& a, const GemmKernelParams& kp, cudaStr
   if (rc) return rc;
   const long long tiles256 = (long long)((a.rows_max + kBM - 1) / kBM) * ((a.N + 255) / 256);
   if (tiles256 < num_sms) return launch_gemm_t<64, EPI>(a, kp, stream);
+  // 256 x 256 tiles on CTA pairs once there is at least a full wave of them.
+  const long long pair_tiles = (long long)((a.rows_max + 2 * kBM - 1) / (2 * kBM)) * ((a.N + 255) / 256);
+  const int clusters = pair_gemm_enabled() ? pair_clusters<EPI>() : 0;
+  if (clusters > 0 && pair_tiles >= clusters)
+    return launch_gemm_pair<EPI>(a, kp, clusters, stream);
   return launch_gemm_t<256, EPI>(a, kp, stream);
 }
 

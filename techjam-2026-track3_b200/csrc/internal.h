@@ -33,6 +33,14 @@ int set_error(int code, const char* fmt, ...);
 
 int ensure_device_props(int* num_sms);
 
+// Index of the current device for per-device caches of launch attributes
+// (call after ensure_device_props, which rejects indices >= 64).
+inline int device_index() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d & 63;
+}
+
 // Number of int32 entries of the token plan for a [B, S] batch.
 int64_t plan_ints(int B, int S);
 

@@ -94,7 +94,9 @@ def _gemm_ref(a16, w16, bias):
 @pytest.mark.parametrize(
     "rows,count,D,H",
     [(128, 128, 256, 4), (1000, 777, 768, 12), (4096, 4096, 1024, 16), (300, 0, 256, 4),
-     (200, 150, 256, 8), (40, 33, 16, 4), (77, 77, 96, 4)],
+     (200, 150, 256, 8), (40, 33, 16, 4), (77, 77, 96, 4),
+     # CTA-pair tiles (256 rows): second CTA partly valid / without valid rows / past rows_max
+     (5000, 4321, 768, 12), (5000, 4196, 768, 12), (4100, 4100, 768, 12)],
 )
 def test_gemm_qkv_headmajor(cuda_pkg, rows, count, D, H):
     """Head-major output [3][H][rows][64]; head dims below 64 zero-padded."""
@@ -119,7 +121,8 @@ def test_gemm_qkv_headmajor(cuda_pkg, rows, count, D, H):
 
 
 @pytest.mark.parametrize("rows,count,N,K",
-                         [(256, 200, 1024, 1024), (1000, 1000, 768, 3072), (640, 513, 256, 256), (40000, 39000, 1024, 1024)])
+                         [(256, 200, 1024, 1024), (1000, 1000, 768, 3072), (640, 513, 256, 256), (40000, 39000, 1024, 1024),
+                          (30000, 29999, 640, 512)])
 def test_gemm_bias_residual_f32(cuda_pkg, rows, count, N, K):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(rows + N + K)
@@ -134,7 +137,8 @@ def test_gemm_bias_residual_f32(cuda_pkg, rows, count, N, K):
     torch.testing.assert_close(out[:count], ref[:count], rtol=1e-4, atol=1e-3)
 
 
-@pytest.mark.parametrize("rows,N,K", [(512, 4096, 1024), (333, 3072, 768), (128, 1024, 256), (100, 136, 96)])
+@pytest.mark.parametrize("rows,N,K", [(512, 4096, 1024), (333, 3072, 768), (128, 1024, 256), (100, 136, 96),
+                                      (9000, 4096, 1024), (12000, 1000, 512)])
 def test_gemm_bias_gelu_f16(cuda_pkg, rows, N, K):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(rows + N)
