@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sV = sK + kKVStages * kKVBytes;  // kKVStages x 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKVStages * kKVBytes);
   // q_full, k_full[4], v_full[4], k_empty[4], v_empty[4], vfix[4],
-  // s_full[2], s_empty[2], p_full[2], pv_done[2], final
+  // s_full[2], s_empty[2], p_full[2], pv_done[2], final, exp_done0[4], exp_done1[4]
   const uint32_t q_full = smem_u32(bars + 0);
   auto k_full = [&](int s) { return smem_u32(bars + 1 + s); };
   auto v_full = [&](int s) { return smem_u32(bars + 5 + s); };
@@ -170,7 +170,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto p_full = [&](int t) { return smem_u32(bars + 25 + t); };
   auto pv_done = [&](int t) { return smem_u32(bars + 27 + t); };
   const uint32_t final_bar = smem_u32(bars + 29);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
+  // exp_done{t}[q]: the softmax warp of query tile t on SM sub-partition q has
+  // issued the exponentials of its current key tile (see the softmax loop).
+  auto exp_done = [&](int t, int q) { return smem_u32(bars + 30 + 4 * t + q); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 38);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_idx();
@@ -192,6 +195,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(pv_done(t), 1);
     }
     mbar_init(final_bar, 1);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(exp_done(0, q), 1);
+      mbar_init(exp_done(1, q), 1);
+    }
     *abort_flag = device_failed() ? 1 : 0;
     fence_barrier_init();
   }
@@ -414,6 +421,52 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
         const float m_cand = fmaxf(m_run, mx * sl2);
 
+        // The running max moves only when it would grow by more than the
+        // threshold; O and the row sum are then rescaled by alpha below.
+        const bool need = __any_sync(0xffffffffu, m_cand > m_run + kRescaleThreshold);
+        float alpha = 1.f;
+        if (need) {
+          alpha = (m_cand == -INFINITY) ? 1.f : exp2_approx(m_run - m_cand);
+          l_run *= alpha;
+          if (m_cand != -INFINITY) m_run = m_cand;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        const float2 sl2v = make_float2(sl2, sl2);
+        const float2 negm = make_float2(-m_use, -m_use);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+        // The two softmax warps of an SM sub-partition (one per query tile)
+        // take turns on the exponentials, tile 0 first: while one holds the
+        // MUFU and FMA pipes, the other loads its next S row and takes its
+        // max, instead of both reaching the exponentials at the same time.
+        if (ntile == 2 && (t == 1 || j >= 1)) {
+          const uint32_t bar = t == 0 ? exp_done(1, quarter) : exp_done(0, quarter);
+          const uint32_t parity = (uint32_t)((t == 0 ? j - 1 : j) & 1);
+          if (!mbar_wait(bar, parity, abort_flag, 223)) {
+            ok = false;
+            break;
+          }
+        }
+        // P is computed into registers first, so the exponentials overlap the
+        // tensor core's P_{j-1} V_{j-1}; only the TMEM stores wait for it.
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          float2 x = ffma2(make_float2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), sl2v, negm);
+          if ((c & 7) < kPolyPairsPer8) {
+            x = exp2_poly2(x);  // FMA pipe
+          } else {
+            x.x = exp2_approx(x.x);  // MUFU
+            x.y = exp2_approx(x.y);
+          }
+          acc[c & 3] = fadd2(acc[c & 3], x);
+          pk[c] = pack_half2(x.x, x.y);
+        }
+        if (ntile == 2) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(exp_done(t, quarter));
+        }
+
         // P_{j-1} V_{j-1} must be done: it reads the P buffer and writes O.
         if (j >= 1) {
           if (!mbar_wait(pv_done(t), (uint32_t)((j - 1) & 1), abort_flag, 221)) {
@@ -421,11 +474,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             break;
           }
           tc_fence_after();
-        }
-        const bool need = __any_sync(0xffffffffu, m_cand > m_run + kRescaleThreshold);
-        if (need) {
-          const float alpha = (m_cand == -INFINITY) ? 1.f : exp2_approx(m_run - m_cand);
-          if (j >= 1) {
+          if (need) {
             uint32_t o[32];
             tmem_ld32(o_tmem, o);
             tmem_ld_wait();
@@ -438,32 +487,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
             tmem_st32(o_tmem + 32u, o);
           }
-          l_run *= alpha;
-          if (m_cand != -INFINITY) m_run = m_cand;
         }
-        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        const float2 sl2v = make_float2(sl2, sl2);
-        const float2 negm = make_float2(-m_use, -m_use);
-        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                         make_float2(0.f, 0.f)};
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int e = half * 64 + 2 * c;
-            float2 x = ffma2(make_float2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), sl2v, negm);
-            if ((c & 7) < kPolyPairsPer8) {
-              x = exp2_poly2(x);  // FMA pipe
-            } else {
-              x.x = exp2_approx(x.x);  // MUFU
-              x.y = exp2_approx(x.y);
-            }
-            acc[c & 3] = fadd2(acc[c & 3], x);
-            pk[c] = pack_half2(x.x, x.y);
-          }
-          tmem_st32(p_tmem + (uint32_t)(half * 32), pk);
-        }
+        tmem_st32(p_tmem, *reinterpret_cast<uint32_t(*)[32]>(pk + 0));
+        tmem_st32(p_tmem + 32u, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
         tmem_st_wait();
         const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
         const float2 a = fadd2(a01, a23);
