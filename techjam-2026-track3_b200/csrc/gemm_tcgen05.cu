@@ -8,7 +8,7 @@
 //                     FFN-out (v16_1_clean.py:533-537 + :621): +bias, +fp32
 //                     residual, fp32 store.
 //   kEpiGeluF16       FFN-in (v16_1_clean.py:221-301, the Triton fused op):
-//                     +bias, exact erf-GELU on the fp32 accumulator, fp16.
+//                     +bias, erf-GELU on the fp32 accumulator, fp16.
 //
 // Structure (one CTA per SM, 64 + 32 * epilogue-warps threads):
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
@@ -54,6 +54,10 @@ struct GemmKernelParams {
   int heads, head_dim, d_model;
 };
 
+// Shared-memory scratch of the epilogue warps (one 32-row block each), used to
+// turn the TMEM layout (thread = row) into row-contiguous global accesses.
+constexpr uint32_t kEpiScratchBytes = 32768;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
@@ -61,12 +65,42 @@ struct GemmCfg {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
-  static constexpr size_t kSmemBytes =
-      1024 /*align slack*/ + (size_t)kStages * kStageBytes + 256 /*barriers etc*/;
+  static constexpr size_t kSmemBytes = 1024 /*align slack*/ + (size_t)kStages * kStageBytes +
+                                       256 /*barriers etc*/ + kEpiScratchBytes;
 };
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+// GELU(x) = x * Phi(x) with Phi(x) = (1 + erf(x / sqrt(2))) / 2 and erf from
+// Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26:
+//   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
+// so Phi(x) = 1 - c/2 for x >= 0 and c/2 for x < 0, c = erfc(|x| / sqrt(2)).
+// Branch-free, on pairs (packed FMA); the absolute error on GELU stays below
+// 5e-7, far under the fp16 rounding of the output.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float2 gelu2(float2 x) {
+  constexpr float kP = 0.3275911f;
+  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f,
+                  kA4 = -1.453152027f, kA5 = 1.061405429f;
+  constexpr float kInvSqrt2 = 0.70710678118654752f;
+  constexpr float kNegLog2e = -1.4426950408889634f;
+  const float2 z = make_float2(fabsf(x.x) * kInvSqrt2, fabsf(x.y) * kInvSqrt2);
+  const float2 den = ffma2(z, make_float2(kP, kP), make_float2(1.f, 1.f));
+  const float2 t = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  float2 q = ffma2(make_float2(kA5, kA5), t, make_float2(kA4, kA4));
+  q = ffma2(q, t, make_float2(kA3, kA3));
+  q = ffma2(q, t, make_float2(kA2, kA2));
+  q = ffma2(q, t, make_float2(kA1, kA1));
+  q = fmul2(q, t);
+  const float2 arg = fmul2(fmul2(z, z), make_float2(kNegLog2e, kNegLog2e));
+  const float2 e = make_float2(exp2_approx(arg.x), exp2_approx(arg.y));
+  const float2 hc = fmul2(fmul2(q, e), make_float2(0.5f, 0.5f));  // erfc(|x|/sqrt2) / 2
+  const float2 phi = make_float2(x.x >= 0.f ? 1.f - hc.x : hc.x, x.y >= 0.f ? 1.f - hc.y : hc.y);
+  return fmul2(x, phi);
 }
 
 // Wait without the CTA abort flag: used on the exit path to let TMA loads or
@@ -78,82 +112,152 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-// Epilogue of one accumulator tile for one epilogue warp: prefetch the
-// residual (before waiting, so its latency hides behind the main loop), wait
-// for the accumulator, then bias + fused op + store for the warp's rows
-// (TMEM lane quarter) and column slice.  Returns false if the CTA aborts.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Epilogue of one accumulator tile for one epilogue warp: its 32 rows (TMEM
+// lane quarter) and its column slice, in 32-column chunks.  Each chunk is
+// read from TMEM with one row per thread, passed through the warp's scratch
+// (16-byte granules XOR-swizzled by row, so neither the row-wise writes nor
+// the column-wise reads conflict) and written with consecutive lanes on
+// consecutive addresses of a row:
+//   fp32 (residual): lane = (row l/8 + 4i, 4 columns), 128 B per row segment;
+//   fp16 (QKV, GELU): lane = (row l/4 + 8i, 8 columns), 64 B per row segment.
+// The residual is prefetched in the store layout before the accumulator is
+// waited for, so its DRAM latency hides behind the tile's main loop.
+// Returns false if the CTA aborts.
 template <int BN, int EPI, int kEpiWarps>
 __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_t tmem_acc, int m0,
                                               int n0, int rows, int quarter, int slice, uint32_t lane,
                                               uint32_t tfull_bar, uint32_t tfull_parity,
-                                              volatile int* abort_flag) {
+                                              volatile int* abort_flag, uint32_t scratch) {
   constexpr int kSlices = kEpiWarps / 4;
   constexpr int kChunks = BN / 32 / kSlices;
-  const int row_in_tile = quarter * 32 + (int)lane;
-      const int row = m0 + row_in_tile;
-      const bool row_ok = row < rows;
-      // Residual rows are fetched before waiting for the accumulator, so their
-      // DRAM latency hides behind the tile's main loop.
-      float4 res[EPI == kEpiResidualF32 ? kChunks : 1][8];
-      if (EPI == kEpiResidualF32) {
-        const int64_t resid_row = row_ok ? (p.resid_map ? (int64_t)p.resid_map[row] : (int64_t)row) : 0;
+  const int row_base = m0 + quarter * 32;
+  const uint32_t t_row = tmem_acc + ((uint32_t)(quarter * 32) << 16);
+
+  if constexpr (EPI == kEpiResidualF32) {
+    const int sub = (int)(lane >> 3);
+    const int c4 = (int)(lane & 7) * 4;
+    int rrow[8];  // residual row of each output row, -1 past the row count
 #pragma unroll
-        for (int cc = 0; cc < kChunks; ++cc) {
-          const int nc = n0 + (slice * kChunks + cc) * 32;
-          const float4* rs = reinterpret_cast<const float4*>(p.resid + resid_row * p.ld_resid + nc);
+    for (int i = 0; i < 8; ++i) {
+      const int row = row_base + sub + 4 * i;
+      rrow[i] = row < rows ? (p.resid_map ? p.resid_map[row] : row) : -1;
+    }
+    float4 res[kChunks][8];
 #pragma unroll
-          for (int g = 0; g < 8; ++g)
-            res[cc][g] = (row_ok && nc + 4 * g < p.N) ? __ldg(rs + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int col = n0 + (slice * kChunks + cc) * 32 + c4;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        res[cc][i] = (rrow[i] >= 0 && col < p.N)
+                         ? __ldg(reinterpret_cast<const float4*>(p.resid + (int64_t)rrow[i] * p.ld_resid + col))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (!mbar_wait(tfull_bar, tfull_parity, abort_flag, 131)) return false;
+    tc_fence_after();
+#pragma unroll
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = slice * kChunks + cc;
+      const int col = n0 + c * 32 + c4;
+      uint32_t r[32];
+      tmem_ld32(t_row + (uint32_t)(c * 32), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        st_shared_v4(scratch + lane * 128 + ((k ^ (lane & 7)) << 4),
+                     make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]));
+      __syncwarp();
+      const float4 b4 = col < p.N ? __ldg(reinterpret_cast<const float4*>(p.bias + col))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t rr = (uint32_t)(sub + 4 * i);
+        const uint4 a = ld_shared_v4(scratch + rr * 128 + (((lane & 7) ^ (rr & 7)) << 4));
+        if (rrow[i] >= 0 && col < p.N) {
+          const float4 rs = res[cc][i];
+          *reinterpret_cast<float4*>(static_cast<float*>(p.out) + (int64_t)(row_base + (int)rr) * p.ld_out + col) =
+              make_float4(__uint_as_float(a.x) + b4.x + rs.x, __uint_as_float(a.y) + b4.y + rs.y,
+                          __uint_as_float(a.z) + b4.z + rs.z, __uint_as_float(a.w) + b4.w + rs.w);
         }
       }
-      if (!mbar_wait(tfull_bar, tfull_parity, abort_flag, 130 + EPI)) return false;
-      tc_fence_after();
-      const uint32_t t_row = tmem_acc + ((uint32_t)(quarter * 32) << 16);
-      // fp16 epilogues load two TMEM chunks per wait; the residual one keeps
-      // 128 registers of prefetched residual and loads one.
-      constexpr int kPerWait = (EPI == kEpiResidualF32 || kChunks < 2) ? 1 : 2;
-      uint32_t rbuf[kPerWait][32];
+      __syncwarp();  // the next chunk reuses the scratch
+    }
+    return true;
+  } else {
+    if (!mbar_wait(tfull_bar, tfull_parity, abort_flag, 130 + EPI)) return false;
+    tc_fence_after();
+    // Two TMEM chunks per wait when the slice has them.
+    constexpr int kPerWait = kChunks < 2 ? 1 : 2;
+    const bool hm_fast = EPI == kEpiQkvHeadMajor && (p.head_dim & 31) == 0;
+    uint32_t rbuf[kPerWait][32];
 #pragma unroll
-      for (int cc = 0; cc < kChunks; ++cc) {
-        const int c = slice * kChunks + cc;
-        if (cc % kPerWait == 0) {
+    for (int cc = 0; cc < kChunks; ++cc) {
+      const int c = slice * kChunks + cc;
+      if (cc % kPerWait == 0) {
 #pragma unroll
-          for (int u = 0; u < kPerWait; ++u) tmem_ld32(t_row + (uint32_t)((c + u) * 32), rbuf[u]);
-          tmem_ld_wait();
+        for (int u = 0; u < kPerWait; ++u) tmem_ld32(t_row + (uint32_t)((c + u) * 32), rbuf[u]);
+        tmem_ld_wait();
+      }
+      const uint32_t (&r)[32] = rbuf[cc % kPerWait];
+      const int nc = n0 + c * 32;
+      if (nc >= p.N) continue;  // uniform for the warp
+      // Bias + op in the TMEM layout (thread = row), packed to fp16.
+      uint32_t pk[16];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int n = nc + 8 * g;
+        float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+        if (n < p.N) {
+          b0 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
+          b1 = __ldg(reinterpret_cast<const float4*>(p.bias + n) + 1);
         }
-        const uint32_t (&r)[32] = rbuf[cc % kPerWait];
-        const int nc = n0 + c * 32;
-        if (!row_ok || nc >= p.N) continue;
+        float2 w[4] = {make_float2(__uint_as_float(r[8 * g + 0]) + b0.x, __uint_as_float(r[8 * g + 1]) + b0.y),
+                       make_float2(__uint_as_float(r[8 * g + 2]) + b0.z, __uint_as_float(r[8 * g + 3]) + b0.w),
+                       make_float2(__uint_as_float(r[8 * g + 4]) + b1.x, __uint_as_float(r[8 * g + 5]) + b1.y),
+                       make_float2(__uint_as_float(r[8 * g + 6]) + b1.z, __uint_as_float(r[8 * g + 7]) + b1.w)};
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int n = nc + 8 * g;
-          if (n >= p.N) break;
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + n) + 1);
-          float w[8] = {__uint_as_float(r[8 * g + 0]) + b0.x, __uint_as_float(r[8 * g + 1]) + b0.y,
-                        __uint_as_float(r[8 * g + 2]) + b0.z, __uint_as_float(r[8 * g + 3]) + b0.w,
-                        __uint_as_float(r[8 * g + 4]) + b1.x, __uint_as_float(r[8 * g + 5]) + b1.y,
-                        __uint_as_float(r[8 * g + 6]) + b1.z, __uint_as_float(r[8 * g + 7]) + b1.w};
-          if (EPI == kEpiQkvHeadMajor) {
-            // Head-major rows are kHeadPad (64) halves; a head dim below 64 is
-            // stored zero-padded, so attention always sees 64-wide rows.
-            __half* qkv = static_cast<__half*>(p.out);
+        for (int u = 0; u < 4; ++u) {
+          if (EPI == kEpiGeluF16) w[u] = gelu2(w[u]);
+          pk[4 * g + u] = pack_half2(w[u].x, w[u].y);
+        }
+      }
+      const int row = row_base + (int)lane;
+      if (EPI == kEpiQkvHeadMajor && !hm_fast) {
+        // Head dims that are not a multiple of 32: head-major addressing per
+        // 8-column group (or per element), one row per thread; padding
+        // columns up to 64 are zeroed by the writer of a head's last column.
+        if (row < rows) {
+          __half* qkv = static_cast<__half*>(p.out);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int n = nc + 8 * g;
+            if (n >= p.N) break;
             if ((p.head_dim & 7) == 0) {
               const int which = n / p.d_model;
               const int rem = n - which * p.d_model;
               const int h = rem / p.head_dim;
               const int d = rem - h * p.head_dim;
               __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
-              uint4 o;
-              o.x = pack_half2(w[0], w[1]);
-              o.y = pack_half2(w[2], w[3]);
-              o.z = pack_half2(w[4], w[5]);
-              o.w = pack_half2(w[6], w[7]);
-              *reinterpret_cast<uint4*>(rowp + d) = o;
+              *reinterpret_cast<uint4*>(rowp + d) = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
               if (d + 8 == p.head_dim)
                 for (int z = p.head_dim; z < kHeadPad; z += 8)
                   *reinterpret_cast<uint4*>(rowp + z) = make_uint4(0u, 0u, 0u, 0u);
             } else {
+#pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int ne = n + e;
                 const int which = ne / p.d_model;
@@ -161,30 +265,49 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
                 const int h = rem / p.head_dim;
                 const int d = rem - h * p.head_dim;
                 __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
-                rowp[d] = __float2half_rn(w[e]);
+                const uint32_t bits = pk[4 * g + (e >> 1)] >> ((e & 1) * 16);
+                rowp[d] = __ushort_as_half((unsigned short)(bits & 0xFFFFu));
                 if (d + 1 == p.head_dim)
                   for (int z = p.head_dim; z < kHeadPad; ++z) rowp[z] = __float2half_rn(0.f);
               }
             }
-          } else if (EPI == kEpiGeluF16) {
-            __half* dst = static_cast<__half*>(p.out) + (int64_t)row * p.ld_out + n;
-            uint4 o;
-            o.x = pack_half2(gelu_erf(w[0]), gelu_erf(w[1]));
-            o.y = pack_half2(gelu_erf(w[2]), gelu_erf(w[3]));
-            o.z = pack_half2(gelu_erf(w[4]), gelu_erf(w[5]));
-            o.w = pack_half2(gelu_erf(w[6]), gelu_erf(w[7]));
-            *reinterpret_cast<uint4*>(dst) = o;
-          } else {
-            const float4 r0 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g];
-            const float4 r1 = res[EPI == kEpiResidualF32 ? cc : 0][2 * g + 1];
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
-                                                    (int64_t)row * p.ld_out + n);
-            dst[0] = make_float4(w[0] + r0.x, w[1] + r0.y, w[2] + r0.z, w[3] + r0.w);
-            dst[1] = make_float4(w[4] + r1.x, w[5] + r1.y, w[6] + r1.z, w[7] + r1.w);
           }
         }
+        continue;
       }
-  return true;
+      // Row-contiguous stores through the scratch: 32 rows x 64 bytes.
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        st_shared_v4(scratch + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4),
+                     make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]));
+      __syncwarp();
+      const uint32_t k = lane & 3;
+      const int col = nc + 8 * (int)k;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t rr = (lane >> 2) + 8 * i;
+        const uint4 v = ld_shared_v4(scratch + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
+        const int orow = row_base + (int)rr;
+        if (orow >= rows || col >= p.N) continue;
+        if (EPI == kEpiGeluF16) {
+          *reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + (int64_t)orow * p.ld_out + col) = v;
+        } else {
+          // A 32-column chunk lies inside one head (head_dim is 32 or 64).
+          const int which = nc / p.d_model;
+          const int rem = nc - which * p.d_model;
+          const int h = rem / p.head_dim;
+          const int d0 = rem - h * p.head_dim;
+          __half* rowp = static_cast<__half*>(p.out) +
+                         ((int64_t)(which * p.heads + h) * p.rows_max + orow) * kHeadPad;
+          *reinterpret_cast<uint4*>(rowp + d0 + 8 * (int)k) = v;
+          if (p.head_dim == 32)
+            *reinterpret_cast<uint4*>(rowp + 32 + 8 * (int)k) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      __syncwarp();  // the next chunk reuses the scratch
+    }
+    return true;
+  }
 }
 
 template <int BN, int EPI>
@@ -203,6 +326,7 @@ __global__ void __launch_bounds__(gemm_threads_for(BN, EPI), 1)
   // bars: full[S], empty[S], tfull[2], tempty[2], final
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t scratch_base = smem_u32(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = warp_idx();
   const uint32_t lane = lane_id();
@@ -328,7 +452,8 @@ __global__ void __launch_bounds__(gemm_threads_for(BN, EPI), 1)
       const int m0 = (t / n_tiles) * kBM;
       const int n0 = (t % n_tiles) * BN;
       if (!epilogue_tile<BN, EPI, kEpiWarps>(p, tmem_base + (uint32_t)(acc * BN), m0, n0, rows, quarter,
-                                             slice, lane, tfull_bar(acc), acc_phase, abort_flag))
+                                             slice, lane, tfull_bar(acc), acc_phase, abort_flag,
+                                             scratch_base + (uint32_t)(warp - 2) * (kEpiScratchBytes / kEpiWarps)))
         break;
       tc_fence_before();
       __syncwarp();
@@ -374,7 +499,7 @@ struct PairCfg {
   static constexpr uint32_t kBBytes = (kBN / 2) * kBK * 2;      // this CTA's 128 rows of W
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kTmemCols = 2 * kBN;
-  static constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
+  static constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256 + kEpiScratchBytes;
 };
 
 template <int EPI>
@@ -394,6 +519,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256
   // bars: full[S] (leader's used), empty[S], tfull[2], tempty[2] (leader's used), final
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t scratch_base = smem_u32(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = warp_idx();
   const uint32_t lane = lane_id();
@@ -525,7 +651,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256
       const int m0 = (t / n_tiles) * (2 * kBM) + (int)rank * kBM;
       const int n0 = (t % n_tiles) * BN;
       if (!epilogue_tile<BN, EPI, kEpiWarps>(p, tmem_base + (uint32_t)(acc * BN), m0, n0, rows, quarter,
-                                             slice, lane, tfull_bar(acc), acc_phase, abort_flag))
+                                             slice, lane, tfull_bar(acc), acc_phase, abort_flag,
+                                             scratch_base + (uint32_t)(warp - 2) * (kEpiScratchBytes / kEpiWarps)))
         break;
       tc_fence_before();
       __syncwarp();
