@@ -457,7 +457,7 @@ __global__ void __launch_bounds__(gemm_threads_for(BN, EPI), 1)
         break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (lane == 0) mbar_arrive_relaxed(tempty_bar(acc));
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -656,7 +656,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256
         break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+      if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(tempty_bar(acc), 0));
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
