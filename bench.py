@@ -481,7 +481,7 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
     ctx = torch.empty(rows, D, dtype=torch.float16, device=device)
     x1 = torch.empty(rows, D, dtype=torch.float32, device=device)
     h16 = torch.empty(rows, F, dtype=torch.float16, device=device)
-    x2 = torch.empty(rows, D, dtype=torch.float32, device=device)
+    y16 = torch.empty(rows, D, dtype=torch.float16, device=device)
     out = torch.empty(rows, D, dtype=torch.float32, device=device)
     xf = x.view(rows, D)
     kv_off = cu[:-1].contiguous()
@@ -495,19 +495,17 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
                                                 cnt.view(-1, 1), S, dh**-0.5, causal=bool(cfg.causal),
                                                 out=ctx, head_dim=dh), "tensor",
                        float(((2.0 * lens * (lens + 1)) if cfg.causal else (4.0 * lens * lens)).mul(D).sum())),
-        "gemm_out_resid": (lambda: k.gemm_bias_residual_f32(ctx, att._out_weight_mixed, att.out_proj.bias, xf,
-                                                            resid_map=orig, row_count=nv_t, out=x1),
-                           "tensor", 2.0 * nv * D * D),
-        "ln2_cast_f16": (lambda: k.ln_cast_f16(x1, layer.norm2.weight, layer.norm2.bias, row_count=nv_t,
-                                               out=a16), "hbm", nv * D * (4 + 2)),
+        "gemm_out_f16": (lambda: k.gemm_bias_f16(ctx, att._out_weight_mixed, att.out_proj.bias, row_count=nv_t,
+                                                 out=y16), "tensor", 2.0 * nv * D * D),
+        "add_ln2_f16": (lambda: k.add_ln_cast_f16(xf, y16, layer.norm2.weight, layer.norm2.bias, row_map=orig,
+                                                  row_count=nv_t, sum_out=x1, out=a16), "hbm", nv * D * (4 + 2 + 4 + 2)),
         "gemm_ffn_in_gelu": (lambda: k.gemm_bias_gelu_f16(a16, layer._ffn_in_weight_mixed, layer.ffn_in.bias,
                                                           row_count=nv_t, out=h16), "tensor", 2.0 * nv * F * D),
-        "gemm_ffn_out_resid": (lambda: k.gemm_bias_residual_f32(h16, layer._ffn_out_weight_mixed,
-                                                                layer.ffn_out.bias, x1, row_count=nv_t, out=x2),
-                               "tensor", 2.0 * nv * D * F),
-        "ln_final_mask": (lambda: k.ln_final_mask(x2, model.final_norm.weight, model.final_norm.bias,
-                                                  inv_map=inv, rows=rows, out=out), "hbm",
-                          nv * D * 8 + (rows - nv) * D * 4),
+        "gemm_ffn_out_f16": (lambda: k.gemm_bias_f16(h16, layer._ffn_out_weight_mixed, layer.ffn_out.bias,
+                                                     row_count=nv_t, out=y16), "tensor", 2.0 * nv * D * F),
+        "add_ln_final_mask": (lambda: k.add_ln_final_mask(x1, y16, model.final_norm.weight, model.final_norm.bias,
+                                                          inv_map=inv, rows=rows, out=out), "hbm",
+                              nv * D * (4 + 2 + 4) + (rows - nv) * D * 4),
     }
     stream = torch.cuda.current_stream(device)
     reps = max(3, min(50, args.steps))

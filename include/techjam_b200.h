@@ -107,6 +107,25 @@ TJ_API int tj_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t*
 TJ_API int tj_ln_final_mask(const float* x, const int32_t* inv_map, int rows, int d_model,
                      const float* gamma, const float* beta, float eps, float* out, void* stream);
 
+/* Residual add fused into the LayerNorm that follows it.  For r < min(rows,
+ * *row_count):
+ *   s = x[row_map ? row_map[r] : r] + float(add16[r])          (fp32)
+ *   sum_out[r] = s   (if sum_out is not NULL)
+ *   y16[r] = fp16(LayerNorm(s))
+ * Replaces `x = x + attention_output` / `x = x + ffn_output` (the branch output
+ * being the fp16 F.linear result .float()) and the norm2 / next layer's norm1
+ * that reads it: v16_1_clean.py:620-621 + :527, :615-616. */
+TJ_API int tj_add_ln_cast_f16(const float* x, const int32_t* row_map, const void* add16,
+                       const int32_t* row_count, int rows, int d_model, const float* gamma,
+                       const float* beta, float eps, float* sum_out, void* y16, void* stream);
+
+/* out[m] = LayerNorm(x[c] + float(add16[c])) with c = inv_map[m] >= 0, else
+ * exact zeros, for m < rows.  Replaces the last layer's `x = x + ffn_output`
+ * with final_norm + masked_fill: v16_1_clean.py:621-627. */
+TJ_API int tj_add_ln_final_mask(const float* x, const void* add16, const int32_t* inv_map, int rows,
+                         int d_model, const float* gamma, const float* beta, float eps, float* out,
+                         void* stream);
+
 /* qkv16 (head-major [3][H][rows_max][dh]) = fp16(a16 @ w_qkv^T + b_qkv) for the
  * first min(rows_max, *row_count) rows; w_qkv is the packed [3D, D] q/k/v
  * weight.  Replaces the packed F.linear + reshape/permute/unbind of
@@ -123,6 +142,13 @@ TJ_API int tj_gemm_bias_residual_f32(const void* a16, const void* w16, const flo
                               const float* resid, const int32_t* resid_map,
                               const int32_t* row_count, int rows_max, int n, int k, float* out,
                               void* stream);
+
+/* out16[r] = fp16(a16[r] @ w^T + bias).  Replaces the fp16 F.linear of the
+ * output projection (v16_1_clean.py:519-523) and of FFN-out (:533-537); the
+ * .float() + residual add is tj_add_ln_cast_f16 / tj_add_ln_final_mask. */
+TJ_API int tj_gemm_bias_f16(const void* a16, const void* w16, const float* bias,
+                     const int32_t* row_count, int rows_max, int n, int k, void* out16,
+                     void* stream);
 
 /* out16[r] = fp16(gelu_erf(a16[r] @ w^T + bias)), GELU evaluated on the fp32
  * accumulator.  Replaces torch.ops.techjam.v16_1_clean_fused_ffn_gelu_no_preround

@@ -75,11 +75,20 @@ SIGNATURES = {
     "tj_token_plan": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     "tj_ln_cast_f16": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
     "tj_ln_final_mask": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
+    "tj_add_ln_cast_f16": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp, c_vp],
+    ),
+    "tj_add_ln_final_mask": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp],
+    ),
     "tj_gemm_qkv_headmajor": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "tj_gemm_bias_residual_f32": (
         c_int,
         [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp],
     ),
+    "tj_gemm_bias_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "tj_gemm_bias_gelu_f16": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "tj_flash_attn_fwd": (
         c_int,

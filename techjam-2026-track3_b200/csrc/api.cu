@@ -68,7 +68,7 @@ static int check_device() {
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct EncoderWorkspace {
-  size_t plan, a16, qkv16, x1, x2, h16, total;
+  size_t plan, a16, qkv16, x1, x2, h16, y16, total;
 };
 
 static bool workspace_layout(const tj_encoder_desc* d, EncoderWorkspace* w) {
@@ -90,6 +90,8 @@ static bool workspace_layout(const tj_encoder_desc* d, EncoderWorkspace* w) {
   off = align_up(off + rows * D * 4, 256);
   w->h16 = off;
   off = align_up(off + rows * F * 2, 256);
+  w->y16 = off;  // fp16 output of the out-projection / FFN-out before its residual add
+  off = align_up(off + rows * D * 2, 256);
   w->total = off;
   return true;
 }
@@ -162,6 +164,28 @@ int tj_ln_final_mask(const float* x, const int32_t* inv_map, int rows, int d_mod
   return finish(launch_ln_final(x, inv_map, rows, d_model, gamma, beta, eps, out, s), s);
 }
 
+int tj_add_ln_cast_f16(const float* x, const int32_t* row_map, const void* add16,
+                       const int32_t* row_count, int rows, int d_model, const float* gamma,
+                       const float* beta, float eps, float* sum_out, void* y16, void* stream) {
+  int rc = check_device();
+  if (rc) return rc;
+  if (!add16) return set_error(TJ_ERR_INVALID_ARGUMENT, "add_ln_cast_f16: null addend");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return finish(launch_ln_cast_f16(x, row_map, row_count, rows, d_model, gamma, beta, eps, y16, s,
+                                   add16, sum_out),
+                s);
+}
+
+int tj_add_ln_final_mask(const float* x, const void* add16, const int32_t* inv_map, int rows,
+                         int d_model, const float* gamma, const float* beta, float eps, float* out,
+                         void* stream) {
+  int rc = check_device();
+  if (rc) return rc;
+  if (!add16) return set_error(TJ_ERR_INVALID_ARGUMENT, "add_ln_final_mask: null addend");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return finish(launch_ln_final(x, inv_map, rows, d_model, gamma, beta, eps, out, s, add16), s);
+}
+
 int tj_gemm_qkv_headmajor(const void* a16, const void* w_qkv16, const float* b_qkv,
                           const int32_t* row_count, int rows_max, int d_model, int num_heads,
                           void* qkv16, void* stream) {
@@ -205,6 +229,25 @@ int tj_gemm_bias_residual_f32(const void* a16, const void* w16, const float* bia
   a.ld_resid = n;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return finish(launch_gemm(kEpiResidualF32, a, s), s);
+}
+
+int tj_gemm_bias_f16(const void* a16, const void* w16, const float* bias,
+                     const int32_t* row_count, int rows_max, int n, int k, void* out16,
+                     void* stream) {
+  int rc = check_device();
+  if (rc) return rc;
+  GemmArgs a{};
+  a.a16 = a16;
+  a.w16 = w16;
+  a.bias = bias;
+  a.row_count = row_count;
+  a.rows_max = rows_max;
+  a.N = n;
+  a.K = k;
+  a.out = out16;
+  a.ld_out = n;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return finish(launch_gemm(kEpiBiasF16, a, s), s);
 }
 
 int tj_gemm_bias_gelu_f16(const void* a16, const void* w16, const float* bias,
@@ -297,15 +340,24 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
   float* x1 = reinterpret_cast<float*>(ws + w.x1);
   float* x2 = reinterpret_cast<float*>(ws + w.x2);
   __half* h16 = reinterpret_cast<__half*>(ws + w.h16);
+  __half* y16 = reinterpret_cast<__half*>(ws + w.y16);
   const int32_t* nv = plan.nv();
 
   rc = launch_token_plan(mask, B, S, plan.base, s);
   if (rc) return rc;
+  // Residual stream (fp32, compact rows): layer 0 reads the input through the
+  // plan's row map; afterwards x1 holds x after attention and x2 the input of
+  // the next layer.  The out-projection and FFN-out leave their fp16 result in
+  // y16 and the next LayerNorm kernel adds it to the stream.
   for (int l = 0; l < d->num_layers; ++l) {
     const tj_layer_weights& L = layers[l];
     const float* xin = (l == 0) ? x : x2;
     const int32_t* in_map = (l == 0) ? plan.orig() : nullptr;
-    rc = launch_ln_cast_f16(xin, in_map, nv, rows, D, L.ln1_gamma, L.ln1_beta, d->ln_eps, a16, s);
+    if (l == 0)
+      rc = launch_ln_cast_f16(x, in_map, nv, rows, D, L.ln1_gamma, L.ln1_beta, d->ln_eps, a16, s);
+    else  // x2 = x1 + FFN-out of the previous layer
+      rc = launch_ln_cast_f16(x1, nullptr, nv, rows, D, L.ln1_gamma, L.ln1_beta, d->ln_eps, a16, s,
+                              y16, x2);
     if (rc) return rc;
     GemmArgs g{};
     g.a16 = a16;
@@ -351,14 +403,13 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     o.rows_max = rows;
     o.N = D;
     o.K = D;
-    o.out = x1;
+    o.out = y16;
     o.ld_out = D;
-    o.resid = xin;
-    o.resid_map = in_map;
-    o.ld_resid = D;
-    rc = launch_gemm(kEpiResidualF32, o, s);
+    rc = launch_gemm(kEpiBiasF16, o, s);
     if (rc) return rc;
-    rc = launch_ln_cast_f16(x1, nullptr, nv, rows, D, L.ln2_gamma, L.ln2_beta, d->ln_eps, a16, s);
+    // x1 = x + attention output; a16 = LN2(x1)
+    rc = launch_ln_cast_f16(xin, in_map, nv, rows, D, L.ln2_gamma, L.ln2_beta, d->ln_eps, a16, s, y16,
+                            x1);
     if (rc) return rc;
     GemmArgs f1{};
     f1.a16 = a16;
@@ -380,15 +431,13 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     f2.rows_max = rows;
     f2.N = D;
     f2.K = F;
-    f2.out = x2;
+    f2.out = y16;
     f2.ld_out = D;
-    f2.resid = x1;
-    f2.resid_map = nullptr;
-    f2.ld_resid = D;
-    rc = launch_gemm(kEpiResidualF32, f2, s);
+    rc = launch_gemm(kEpiBiasF16, f2, s);
     if (rc) return rc;
   }
-  rc = launch_ln_final(x2, plan.inv(), rows, D, final_gamma, final_beta, d->ln_eps, out, s);
+  // out = final LN(x1 + FFN-out), scattered to the original rows
+  rc = launch_ln_final(x1, plan.inv(), rows, D, final_gamma, final_beta, d->ln_eps, out, s, y16);
   return finish(rc, s);
 }
 

@@ -9,6 +9,10 @@
 //                     residual, fp32 store.
 //   kEpiGeluF16       FFN-in (v16_1_clean.py:221-301, the Triton fused op):
 //                     +bias, erf-GELU on the fp32 accumulator, fp16.
+//   kEpiBiasF16       output projection (v16_1_clean.py:519-523) and FFN-out
+//                     (v16_1_clean.py:533-537): +bias, fp16, as the reference's
+//                     F.linear in fp16; the residual add happens in the
+//                     LayerNorm kernel that reads the result.
 //
 // Structure (one CTA per SM, 64 + 32 * epilogue-warps threads):
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
@@ -289,7 +293,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
         const uint4 v = ld_shared_v4(scratch + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
         const int orow = row_base + (int)rr;
         if (orow >= rows || col >= p.N) continue;
-        if (EPI == kEpiGeluF16) {
+        if (EPI != kEpiQkvHeadMajor) {
           *reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + (int64_t)orow * p.ld_out + col) = v;
         } else {
           // A 32-column chunk lies inside one head (head_dim is 32 or 64).
@@ -873,6 +877,10 @@ int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
       if (a.ld_out % 8 != 0)
         return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_gelu_f16: ld_out must be a multiple of 8");
       return launch_gemm_bn<kEpiGeluF16>(a, kp, stream);
+    case kEpiBiasF16:
+      if (a.ld_out % 8 != 0)
+        return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_f16: ld_out must be a multiple of 8");
+      return launch_gemm_bn<kEpiBiasF16>(a, kp, stream);
     default:
       return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epilogue);
   }

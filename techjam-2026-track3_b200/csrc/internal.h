@@ -62,17 +62,21 @@ struct PlanView {
 
 int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStream_t stream);
 
+// add16 (optional, fp16, compact rows) is added to the x row before the
+// LayerNorm; sum_out (optional) receives that fp32 sum.
 int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* row_count, int rows,
                        int D, const float* gamma, const float* beta, float eps, void* y16,
-                       cudaStream_t stream);
+                       cudaStream_t stream, const void* add16 = nullptr, float* sum_out = nullptr);
 
 int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
-                    const float* beta, float eps, float* out, cudaStream_t stream);
+                    const float* beta, float eps, float* out, cudaStream_t stream,
+                    const void* add16 = nullptr);
 
 enum GemmEpilogue : int {
   kEpiQkvHeadMajor = 0,   // fp16 out, head-major [3][H][rows_max][dh]
   kEpiResidualF32 = 1,    // fp32 out = acc + bias + residual[row_map(row)]
   kEpiGeluF16 = 2,        // fp16 out = gelu_erf(acc + bias)
+  kEpiBiasF16 = 3,        // fp16 out = acc + bias
 };
 
 struct GemmArgs {

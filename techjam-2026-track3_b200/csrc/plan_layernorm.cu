@@ -139,11 +139,34 @@ __device__ __forceinline__ void ln_row_stats(const float4 (&v)[VPL], int D, int 
   rstd = 1.0f / sqrtf(q / (float)D + eps);
 }
 
+// v[i] += the four fp16 values of group g of an addend row (fp32 sum).
+template <int VPL>
+__device__ __forceinline__ void add_f16_row(float4 (&v)[VPL], const __half* add_row, int D, int lane) {
+  const uint2* ar = reinterpret_cast<const uint2*>(add_row);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int g = i * 32 + lane;
+    if (g * 4 < D) {
+      const uint2 u = __ldg(ar + g);
+      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      v[i].x += lo.x;
+      v[i].y += lo.y;
+      v[i].z += hi.x;
+      v[i].w += hi.y;
+    }
+  }
+}
+
+// y[r] = fp16(LayerNorm(x[row_map[r]] (+ add16[r]))), and with sum_out the
+// fp32 row x[row_map[r]] + add16[r] is stored to sum_out[r] (the residual
+// stream after a branch whose output the GEMM left in fp16).
 template <int VPL>
 __global__ void __launch_bounds__(256) ln_cast_f16_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ row_map,
-    const int32_t* __restrict__ row_count, int rows, int D, const float* __restrict__ gamma,
-    const float* __restrict__ beta, float eps, __half* __restrict__ y) {
+    const __half* __restrict__ add16, const int32_t* __restrict__ row_count, int rows, int D,
+    const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+    float* __restrict__ sum_out, __half* __restrict__ y) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   pdl_wait();
@@ -157,6 +180,15 @@ __global__ void __launch_bounds__(256) ln_cast_f16_kernel(
   for (int i = 0; i < VPL; ++i) {
     const int g = i * 32 + lane;
     v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (add16) add_f16_row<VPL>(v, add16 + (int64_t)row * D, D, lane);
+  if (sum_out) {
+    float4* sr = reinterpret_cast<float4*>(sum_out + (int64_t)row * D);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int g = i * 32 + lane;
+      if (g * 4 < D) sr[g] = v[i];
+    }
   }
   float mean, rstd;
   ln_row_stats<VPL>(v, D, lane, mean, rstd, eps);
@@ -177,6 +209,7 @@ __global__ void __launch_bounds__(256) ln_cast_f16_kernel(
 
 template <int VPL>
 __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__ x,
+                                                       const __half* __restrict__ add16,
                                                        const int32_t* __restrict__ inv_map,
                                                        int rows, int D,
                                                        const float* __restrict__ gamma,
@@ -204,6 +237,7 @@ __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__
     const int g = i * 32 + lane;
     v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  if (add16) add_f16_row<VPL>(v, add16 + src * D, D, lane);
   float mean, rstd;
   ln_row_stats<VPL>(v, D, lane, mean, rstd, eps);
 #pragma unroll
@@ -237,22 +271,24 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* row_count, int rows,
                        int D, const float* gamma, const float* beta, float eps, void* y16,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const void* add16, float* sum_out) {
   if (rows < 0 || D <= 0 || D % 4 != 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
   const int vpl = ln_vpl(D);
   if (vpl < 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_cast_f16: D=%d above 4096", D);
   if (!x || !gamma || !beta || !y16 || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
-      (reinterpret_cast<uintptr_t>(y16) & 7u))
+      (reinterpret_cast<uintptr_t>(y16) & 7u) || (reinterpret_cast<uintptr_t>(add16) & 7u) ||
+      !aligned16(sum_out))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: null or misaligned pointer");
   if (rows == 0) return TJ_OK;
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
   __half* y = static_cast<__half*>(y16);
+  const __half* add = static_cast<const __half*>(add16);
   cudaError_t e = cudaSuccess;
   switch (vpl) {
 #define TJ_LN_CASE(V) \
-  case V: e = launch_pdl(ln_cast_f16_kernel<V>, grid, dim3(warps * 32), 0, stream, x, row_map, row_count, rows, D, gamma, beta, eps, y); break;
+  case V: e = launch_pdl(ln_cast_f16_kernel<V>, grid, dim3(warps * 32), 0, stream, x, row_map, add, row_count, rows, D, gamma, beta, eps, sum_out, y); break;
     TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
 #undef TJ_LN_CASE
   }
@@ -262,21 +298,23 @@ int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* ro
 }
 
 int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
-                    const float* beta, float eps, float* out, cudaStream_t stream) {
+                    const float* beta, float eps, float* out, cudaStream_t stream,
+                    const void* add16) {
   if (rows < 0 || D <= 0 || D % 4 != 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
   const int vpl = ln_vpl(D);
   if (vpl < 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_final_mask: D=%d above 4096", D);
   if (!x || !gamma || !beta || !out || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
-      !aligned16(out))
+      !aligned16(out) || (reinterpret_cast<uintptr_t>(add16) & 7u))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: null or misaligned pointer");
   if (rows == 0) return TJ_OK;
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
+  const __half* add = static_cast<const __half*>(add16);
   cudaError_t e = cudaSuccess;
   switch (vpl) {
 #define TJ_LN_CASE(V) \
-  case V: e = launch_pdl(ln_final_kernel<V>, grid, dim3(warps * 32), 0, stream, x, inv_map, rows, D, gamma, beta, eps, out); break;
+  case V: e = launch_pdl(ln_final_kernel<V>, grid, dim3(warps * 32), 0, stream, x, add, inv_map, rows, D, gamma, beta, eps, out); break;
     TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
 #undef TJ_LN_CASE
   }

@@ -109,6 +109,56 @@ def ln_final_mask(x, gamma, beta, eps=1e-5, inv_map=None, rows=None, out=None):
     return out
 
 
+def add_ln_cast_f16(x, add16, gamma, beta, eps=1e-5, row_map=None, row_count=None, sum_out=None,
+                    out=None):
+    """s = x[row_map[r]] + add16[r] (fp32); sum_out[r] = s; out[r] = fp16(LayerNorm(s))."""
+    dev = x.device
+    _require(x, "x", torch.float32, dev)
+    _require(add16, "add16", torch.float16, dev)
+    D = x.shape[-1]
+    rows = x.numel() // D if row_map is None else row_map.numel()
+    if add16.dim() != 2 or add16.shape[1] != D or add16.shape[0] < rows:
+        raise ValueError(f"add16 must be [>= {rows}, {D}], got {tuple(add16.shape)}")
+    if out is None:
+        out = torch.empty(rows, D, dtype=torch.float16, device=dev)
+    if out.dim() != 2 or out.shape[1] != D or out.shape[0] < rows:
+        raise ValueError(f"out must be [>= {rows}, {D}], got {tuple(out.shape)}")
+    _require(out, "out", torch.float16, dev)
+    if sum_out is not None:
+        _require(sum_out, "sum_out", torch.float32, dev)
+        if sum_out.dim() != 2 or sum_out.shape[1] != D or sum_out.shape[0] < rows:
+            raise ValueError(f"sum_out must be [>= {rows}, {D}], got {tuple(sum_out.shape)}")
+    lib = _lib.load()
+    rc = lib.tj_add_ln_cast_f16(
+        x.data_ptr(), _ptr(row_map), add16.data_ptr(), _ptr(row_count), rows, D, gamma.data_ptr(),
+        beta.data_ptr(), float(eps), _ptr(sum_out), out.data_ptr(), _stream(x),
+    )
+    _lib.check(rc, "add_ln_cast_f16")
+    return out
+
+
+def add_ln_final_mask(x, add16, gamma, beta, eps=1e-5, inv_map=None, rows=None, out=None):
+    """out[m] = LayerNorm(x[c] + add16[c]), c = inv_map[m] (zeros where c < 0)."""
+    dev = x.device
+    _require(x, "x", torch.float32, dev)
+    _require(add16, "add16", torch.float16, dev)
+    D = x.shape[-1]
+    if add16.shape != x.shape:
+        raise ValueError(f"add16 must match x {tuple(x.shape)}, got {tuple(add16.shape)}")
+    if rows is None:
+        rows = x.numel() // D if inv_map is None else inv_map.numel()
+    if out is None:
+        out = torch.empty(rows, D, dtype=torch.float32, device=dev)
+    _require_out(out, "out", (rows, D), torch.float32, dev)
+    lib = _lib.load()
+    rc = lib.tj_add_ln_final_mask(
+        x.data_ptr(), add16.data_ptr(), _ptr(inv_map), rows, D, gamma.data_ptr(), beta.data_ptr(),
+        float(eps), out.data_ptr(), _stream(x),
+    )
+    _lib.check(rc, "add_ln_final_mask")
+    return out
+
+
 def gemm_qkv_headmajor(a16, w_qkv16, b_qkv, num_heads, row_count=None, out=None):
     dev = a16.device
     _require(a16, "a16", torch.float16, dev)
@@ -155,6 +205,28 @@ def gemm_bias_residual_f32(a16, w16, bias, resid, resid_map=None, row_count=None
         _ptr(row_count), rows, N, K, out.data_ptr(), _stream(a16),
     )
     _lib.check(rc, "gemm_bias_residual_f32")
+    return out
+
+
+def gemm_bias_f16(a16, w16, bias, row_count=None, out=None):
+    """fp16 out = a16 @ w16^T + bias (the reference's fp16 F.linear)."""
+    dev = a16.device
+    _require(a16, "a16", torch.float16, dev)
+    _require(w16, "w16", torch.float16, dev)
+    _require(bias, "bias", torch.float32, dev)
+    rows, K = a16.shape
+    N = w16.shape[0]
+    if w16.shape[1] != K:
+        raise ValueError("w16 inner dimension does not match a16")
+    if out is None:
+        out = torch.empty(rows, N, dtype=torch.float16, device=dev)
+    _require_out(out, "out", (rows, N), torch.float16, dev)
+    lib = _lib.load()
+    rc = lib.tj_gemm_bias_f16(
+        a16.data_ptr(), w16.data_ptr(), bias.data_ptr(), _ptr(row_count), rows, N, K, out.data_ptr(),
+        _stream(a16),
+    )
+    _lib.check(rc, "gemm_bias_f16")
     return out
 
 

@@ -151,30 +151,36 @@ class ContextParallelEncoder:
         kv_all = torch.empty(self.world, 2, H, slab, 64, dtype=torch.float16, device=dev)
         ctx = torch.empty(slab, D, dtype=torch.float16, device=dev)
         h16 = torch.empty(slab, F, dtype=torch.float16, device=dev)
+        y16 = torch.empty(Sl, D, dtype=torch.float16, device=dev)
+        x1 = torch.empty(Sl, D, dtype=torch.float32, device=dev)
+        x2 = torch.empty(Sl, D, dtype=torch.float32, device=dev)
 
-        # Layer 0 reads x through the plan's gather map; later layers read the
-        # previous layer's compact output.  GEMM outputs only reach the first
-        # nv (<= S_r) rows, so the fp32 buffers hold S_r rows.
-        xin, in_map = x, orig
-        for layer in m.layers:
+        # Residual stream as in tj_encoder_forward: layer 0 reads x through the
+        # plan's gather map; the out-projection and FFN-out write fp16 (y16) and
+        # the next LayerNorm adds them to the fp32 stream (x1 after attention,
+        # x2 = input of the next layer).  GEMM outputs only reach the first nv
+        # (<= S_r) rows, so the fp32 buffers hold S_r rows.
+        for i, layer in enumerate(m.layers):
             att = layer.attention
-            x1 = torch.empty(Sl, D, dtype=torch.float32, device=dev)
-            x2 = torch.empty(Sl, D, dtype=torch.float32, device=dev)
-            kernels.ln_cast_f16(xin, layer.norm1.weight, layer.norm1.bias, layer.norm1.eps,
-                                row_map=in_map, row_count=nv, out=a16)
+            if i == 0:
+                xin, in_map = x, orig
+                kernels.ln_cast_f16(x, layer.norm1.weight, layer.norm1.bias, layer.norm1.eps,
+                                    row_map=orig, row_count=nv, out=a16)
+            else:
+                xin, in_map = x2, None
+                kernels.add_ln_cast_f16(x1, y16, layer.norm1.weight, layer.norm1.bias, layer.norm1.eps,
+                                        row_count=nv, sum_out=x2, out=a16)
             kernels.gemm_qkv_headmajor(a16, att._qkv_weight_mixed, att._qkv_bias_mixed, H,
                                        row_count=nv, out=qkv)
             dist.all_gather_into_tensor(kv_all.view(-1), qkv[1:3].reshape(-1), group=self.group)
             kernels.flash_attn_fwd(qkv[0], kv_all[:, 0], kv_all[:, 1], cu, kv_off, kv_len, Sl, att.scale,
                                    causal=bool(cfg.causal), q_pos0=q_pos0, out=ctx, head_dim=dh)
-            kernels.gemm_bias_residual_f32(ctx, att._out_weight_mixed, att.out_proj.bias, xin,
-                                           resid_map=in_map, row_count=nv, out=x1)
-            kernels.ln_cast_f16(x1, layer.norm2.weight, layer.norm2.bias, layer.norm2.eps, row_count=nv,
-                                out=a16)
+            kernels.gemm_bias_f16(ctx[:Sl], att._out_weight_mixed, att.out_proj.bias, row_count=nv, out=y16)
+            kernels.add_ln_cast_f16(xin, y16, layer.norm2.weight, layer.norm2.bias, layer.norm2.eps,
+                                    row_map=in_map, row_count=nv, sum_out=x1, out=a16)
             kernels.gemm_bias_gelu_f16(a16, layer._ffn_in_weight_mixed, layer.ffn_in.bias, row_count=nv, out=h16)
-            kernels.gemm_bias_residual_f32(h16, layer._ffn_out_weight_mixed, layer.ffn_out.bias, x1,
-                                           row_count=nv, out=x2)
-            xin, in_map = x2, None
-        out = kernels.ln_final_mask(xin, m.final_norm.weight, m.final_norm.bias, m.final_norm.eps,
-                                    inv_map=inv, rows=Sl)
+            kernels.gemm_bias_f16(h16[:Sl], layer._ffn_out_weight_mixed, layer.ffn_out.bias, row_count=nv,
+                                  out=y16)
+        out = kernels.add_ln_final_mask(x1, y16, m.final_norm.weight, m.final_norm.bias, m.final_norm.eps,
+                                        inv_map=inv, rows=Sl)
         return out.view(1, Sl, D)

@@ -87,6 +87,39 @@ def test_ln_cast_and_final(cuda_pkg, rows, D):
     assert torch.count_nonzero(out[~valid]) == 0
 
 
+@pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (513, 1024), (64, 4096)])
+def test_add_ln_cast_and_final(cuda_pkg, rows, D):
+    """Residual add (fp32 x + fp16 branch output) fused into the LayerNorm."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(rows * 3 + D)
+    x = torch.randn(rows + 5, D, generator=g) * 3 + 0.5
+    add = (torch.randn(rows, D, generator=g) * 2).half()
+    gamma = 1 + 0.1 * torch.randn(D, generator=g)
+    beta = 0.1 * torch.randn(D, generator=g)
+    perm = torch.randperm(rows + 5, generator=g)[:rows].int()
+    cnt = rows - rows // 4
+    s_ref = x[perm.long()] + add.float()  # fp32, the reference's `x + out.float()`
+    ref = torch.nn.functional.layer_norm(s_ref.double(), (D,), gamma.double(), beta.double(), 1e-5)
+    xd, ad, gd, bd = x.to(DEV), add.to(DEV), gamma.to(DEV), beta.to(DEV)
+    sum_out = torch.full((rows, D), float("nan"), device=DEV)
+    y16 = k.add_ln_cast_f16(xd, ad, gd, bd, row_map=perm.to(DEV),
+                            row_count=torch.tensor([cnt], dtype=torch.int32, device=DEV),
+                            sum_out=sum_out).cpu().double()
+    assert torch.equal(sum_out[:cnt].cpu(), s_ref[:cnt]), "fp32 residual sum must be exact"
+    assert torch.isnan(sum_out[cnt:].cpu()).all(), "rows past the count must not be written"
+    assert torch.all((y16[:cnt] - ref[:cnt]).abs() <= ref[:cnt].abs() * 2**-10 + 1e-5)
+    # final LN of x + add, scattered through an inverse map with padded rows
+    xc = x[:rows].contiguous()
+    s2 = xc + add.float()
+    ref2 = torch.nn.functional.layer_norm(s2.double(), (D,), gamma.double(), beta.double(), 1e-5)
+    inv = torch.full((rows + 7,), -1, dtype=torch.int32)
+    slots = torch.randperm(rows + 7, generator=g)[:rows]
+    inv[slots] = torch.arange(rows, dtype=torch.int32)
+    out = k.add_ln_final_mask(xc.to(DEV), ad, gd, bd, inv_map=inv.to(DEV)).cpu().double()
+    torch.testing.assert_close(out[slots], ref2, rtol=0, atol=2e-5)
+    assert torch.count_nonzero(out[inv < 0]) == 0
+
+
 def _gemm_ref(a16, w16, bias):
     return a16.float() @ w16.float().t() + bias
 
@@ -148,6 +181,23 @@ def test_gemm_bias_gelu_f16(cuda_pkg, rows, N, K):
     out = k.gemm_bias_gelu_f16(a, w, b).float()
     ref = torch.nn.functional.gelu(_gemm_ref(a, w, b), approximate="none")
     assert torch.all((out - ref).abs() <= ref.abs() * 2**-10 + 2e-3), float((out - ref).abs().max())
+
+
+@pytest.mark.parametrize("rows,count,N,K", [(300, 300, 1024, 1024), (1000, 777, 136, 96),
+                                           (12416, 12000, 1024, 1024), (9000, 9000, 1000, 4096)])
+def test_gemm_bias_f16(cuda_pkg, rows, count, N, K):
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(rows + N + K + 1)
+    a = torch.randn(rows, K, generator=g).half().to(DEV)
+    w = (torch.randn(N, K, generator=g) / math.sqrt(K)).half().to(DEV)
+    b = torch.randn(N, generator=g).to(DEV)
+    out = torch.full((rows, N), float("nan"), dtype=torch.float16, device=DEV)
+    k.gemm_bias_f16(a, w, b, row_count=torch.tensor([count], dtype=torch.int32, device=DEV), out=out)
+    ref = _gemm_ref(a, w, b)[:count]
+    got = out[:count].float()
+    assert torch.all((got - ref).abs() <= ref.abs() * 2**-10 + 2e-3), float((got - ref).abs().max())
+    if count < rows:
+        assert torch.isnan(out[count:].float()).all(), "rows past the count must not be written"
 
 
 def _attn_ref(q, k, v, q_cu, kv_off, kv_len, scale, causal=False, dh=64):
