@@ -507,7 +507,6 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
                                                           inv_map=inv, rows=rows, out=out), "hbm",
                               nv * D * (4 + 2 + 4) + (rows - nv) * D * 4),
     }
-    stream = torch.cuda.current_stream(device)
     reps = max(3, min(50, args.steps))
     res = {}
     with torch.inference_mode():
@@ -515,12 +514,22 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
             fn()
             fn()
             torch.cuda.synchronize(device)
+            # The reps launches replay from one CUDA graph, so host launch cost
+            # (a ctypes call per launch) does not hide the device time of the
+            # short kernels.
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize(device)
+            stream = torch.cuda.current_stream(device)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
-            for _ in range(reps):
-                fn()
+            graph.replay()
             e.record(stream)
             torch.cuda.synchronize(device)
+            del graph
             ms = s.elapsed_time(e) / reps
             res[name] = {"ms": ms, "bound": bound, "work": work,
                          "rate": work / (ms / 1e3) / (1e12 if bound == "tensor" else 1e9),

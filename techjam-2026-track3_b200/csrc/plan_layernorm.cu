@@ -22,12 +22,29 @@ namespace tj {
 
 // ---------------------------------------------------------------------------
 // Token plan: one CTA of 1024 threads = 32 warps.  Warp w owns a contiguous
-// segment of the B*S mask bytes and reads it 32 bytes at a time (coalesced);
-// a ballot gives the valid lanes, popc their rank.  Pass 1 counts each
-// segment, a scan of the 32 counts gives each warp its first compact row, and
-// pass 2 re-reads the segment and writes orig/inv/cu coalesced.
+// segment of the B*S mask bytes and reads it 32 bytes at a time (coalesced),
+// 16 groups per batch with every load issued before the first is used; a
+// ballot gives the valid lanes, popc their rank.  Pass 1 counts each segment,
+// a scan of the 32 counts gives each warp its first compact row, and pass 2
+// re-reads the segment and writes orig/inv/cu coalesced.
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanBatch = 16;  // 32-byte groups loaded per batch
+
+// Valid flags of groups g0 .. g0+15 of the warp's segment, bit k for group k.
+__device__ __forceinline__ uint32_t plan_load_batch(const uint8_t* __restrict__ mask, int g0, int end,
+                                                     int lane) {
+  uint8_t v[kPlanBatch];
+#pragma unroll
+  for (int k = 0; k < kPlanBatch; ++k) {
+    const int i = g0 + 32 * k + lane;
+    v[k] = (i < end) ? (mask ? __ldg(mask + i) : (uint8_t)1) : (uint8_t)0;
+  }
+  uint32_t bits = 0;
+#pragma unroll
+  for (int k = 0; k < kPlanBatch; ++k) bits |= (v[k] != 0 ? 1u : 0u) << k;
+  return bits;
+}
 
 __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t* __restrict__ mask,
                                                                   int B, int S,
@@ -45,9 +62,10 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
   int32_t* inv = orig + total;
 
   int count = 0;
-  for (int i = begin + lane; i - lane < end; i += 32) {
-    const bool valid = i < end && (mask == nullptr || mask[i] != 0);
-    count += __popc(__ballot_sync(0xffffffffu, valid));
+  for (int g0 = begin; g0 < end; g0 += 32 * kPlanBatch) {
+    const uint32_t bits = plan_load_batch(mask, g0, end, lane);
+#pragma unroll
+    for (int k = 0; k < kPlanBatch; ++k) count += __popc(__ballot_sync(0xffffffffu, (bits >> k) & 1u));
   }
   __shared__ int warp_base[32];
   if (lane == 0) warp_base[warp] = count;
@@ -69,27 +87,33 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
   __syncthreads();
   int run = warp_base[warp];
   int next_start = (begin + S - 1) / S * S;  // first sample start at or after `begin`
-  for (int i = begin + lane; i - lane < end; i += 32) {
-    const bool in = i < end;
-    const bool valid = in && (mask == nullptr || mask[i] != 0);
-    const unsigned bal = __ballot_sync(0xffffffffu, valid);
-    const int rank = __popc(bal & ((1u << lane) - 1u));
-    // Samples starting inside this 32-element group (several when S < 32).
-    const int group0 = i - lane;
-    while (next_start < group0 + 32 && next_start < end) {
-      const int k = next_start - group0;  // lane holding the sample start
-      if (lane == k) cu[next_start / S] = run + rank;
-      next_start += S;
-    }
-    if (in) {
-      if (valid) {
-        orig[run + rank] = i;
-        inv[i] = run + rank;
-      } else {
-        inv[i] = -1;
+  for (int g0 = begin; g0 < end; g0 += 32 * kPlanBatch) {
+    const uint32_t bits = plan_load_batch(mask, g0, end, lane);
+#pragma unroll
+    for (int k = 0; k < kPlanBatch; ++k) {
+      const int group0 = g0 + 32 * k;
+      if (group0 >= end) break;  // uniform for the warp
+      const int i = group0 + lane;
+      const bool in = i < end;
+      const bool valid = ((bits >> k) & 1u) != 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, valid);
+      const int rank = __popc(bal & ((1u << lane) - 1u));
+      // Samples starting inside this 32-element group (several when S < 32).
+      while (next_start < group0 + 32 && next_start < end) {
+        const int kk = next_start - group0;  // lane holding the sample start
+        if (lane == kk) cu[next_start / S] = run + rank;
+        next_start += S;
       }
+      if (in) {
+        if (valid) {
+          orig[run + rank] = i;
+          inv[i] = run + rank;
+        } else {
+          inv[i] = -1;
+        }
+      }
+      run += __popc(bal);
     }
-    run += __popc(bal);
   }
   __syncthreads();
   __threadfence_block();
