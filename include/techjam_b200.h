@@ -25,8 +25,9 @@
  *   mask            uint8/bool [B, S], nonzero = valid token (may be NULL)
  *   weights         float16 [N, K] (nn.Linear layout), biases float32 [N]
  *   LayerNorm       gamma/beta float32 [D], eps as given (nn.LayerNorm: 1e-5)
- *   qkv (head-major) float16 [3][H][rows][64]; a head dim below 64 is stored
- *                   zero-padded to 64 (head dims above 64 are not supported)
+ *   qkv (head-major) float16 [3][H][rows][P] with P = 64, 128 or 256, the
+ *                   smallest that holds the head dim (1..256); each head's
+ *                   row is its head_dim values then zeros up to P
  *   ctx             float16 [rows][D]
  *   "compact rows"  the valid tokens of the batch packed densely in
  *                   (sample, position) order, as the token plan defines.
@@ -126,7 +127,7 @@ TJ_API int tj_add_ln_final_mask(const float* x, const void* add16, const int32_t
                          int d_model, const float* gamma, const float* beta, float eps, float* out,
                          void* stream);
 
-/* qkv16 (head-major [3][H][rows_max][dh]) = fp16(a16 @ w_qkv^T + b_qkv) for the
+/* qkv16 (head-major [3][H][rows_max][P], see above) = fp16(a16 @ w_qkv^T + b_qkv) for the
  * first min(rows_max, *row_count) rows; w_qkv is the packed [3D, D] q/k/v
  * weight.  Replaces the packed F.linear + reshape/permute/unbind of
  * v16_1_clean.py:474-489. */
@@ -157,9 +158,10 @@ TJ_API int tj_gemm_bias_gelu_f16(const void* a16, const void* w16, const float* 
                           const int32_t* row_count, int rows_max, int n, int k, void* out16,
                           void* stream);
 
-/* Masked multi-head attention over compact rows, head_dim 1..64.
- *   q16       [H][q_rows][64] (head_dim values then zeros up to 64)
- *   k16, v16  addressed as [G][H][kv_rows][64] with element strides
+/* Masked multi-head attention over compact rows, head_dim 1..256.
+ *   q16       [H][q_rows][P] (head_dim values then zeros up to P = 64, 128
+ *             or 256, the smallest that holds head_dim)
+ *   k16, v16  addressed as [G][H][kv_rows][P] with element strides
  *             kv_stride_h (between heads) and kv_stride_g (between segments)
  *   q_cu      [batch+1]: queries of sample b are q rows [q_cu[b], q_cu[b+1])
  *   kv_off, kv_len [batch*G]: keys of sample b are, for g = 0..G-1 in order,

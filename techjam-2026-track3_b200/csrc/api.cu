@@ -82,8 +82,8 @@ static bool workspace_layout(const tj_encoder_desc* d, EncoderWorkspace* w) {
   off = align_up(off + (size_t)plan_ints(d->batch, d->seq_len) * 4, 256);
   w->a16 = off;
   off = align_up(off + rows * D * 2, 256);
-  w->qkv16 = off;  // head-major [3][H][rows][64]: heads below 64 are zero-padded
-  off = align_up(off + 3 * rows * (size_t)d->num_heads * 64 * 2, 256);
+  w->qkv16 = off;  // head-major [3][H][rows][P], heads zero-padded to P = 64, 128 or 256
+  off = align_up(off + 3 * rows * (size_t)d->num_heads * attn_head_pad(d->d_model / d->num_heads) * 2, 256);
   w->x1 = off;
   off = align_up(off + rows * D * 4, 256);
   w->x2 = off;
@@ -326,9 +326,9 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
   if (x == out) return set_error(TJ_ERR_INVALID_ARGUMENT, "encoder_forward: x and out alias");
   const int D = d->d_model, H = d->num_heads, F = d->ffn_dim, B = d->batch, S = d->seq_len;
   const int dh = D / H;
-  if (dh > 64)
-    return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: head_dim %d (1..64 supported)", dh);
-  constexpr int kPad = 64;  // head-major row length of the QKV buffer
+  if (dh > 256)
+    return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: head_dim %d (1..256 supported)", dh);
+  const int kPad = attn_head_pad(dh);  // head-major row length of the QKV buffer
   if ((int64_t)B * S > INT32_MAX / 4)
     return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: B*S too large");
   const int rows = B * S;

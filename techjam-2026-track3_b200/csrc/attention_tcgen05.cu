@@ -37,14 +37,34 @@ int make_tmap_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* 
                   const uint64_t* strides_elems, const uint32_t* box);
 
 constexpr int kAttnThreads = 384;
-constexpr int kAttnBM = 128;     // queries per tile (2 tiles per CTA)
-constexpr int kAttnBN = 128;     // keys per tile
-constexpr int kDH = 64;          // head dim
-constexpr int kKVStages = 4;
-constexpr uint32_t kQBytes = kAttnBM * kDH * 2;   // 16 KB
-constexpr uint32_t kKVBytes = kAttnBN * kDH * 2;  // 16 KB
-constexpr size_t kAttnSmem = 1024 + 2 * kQBytes + 2 * kKVStages * kKVBytes + 512;
+constexpr int kAttnBM = 128;     // queries per tile
 constexpr uint32_t kAttnTmemCols = 512;
+
+// Per padded head dim DH (the q/k/v row length: 64, 128 or 256; head dims
+// below it are zero-padded): 64-column chunks CH (one 128-byte swizzle atom
+// each), keys per tile BN, query tiles per CTA NT and K/V pipeline stages,
+// chosen so shared memory (<= 227 KB) and TMEM (512 columns) hold them.
+// TMEM per query tile: O [0, DH), S [DH, DH+BN), P [DH+BN, DH+BN+BN/2) (fp16
+// pairs); DH=64 packs two tiles at a 256-column stride.
+template <int DH_>
+struct AttnCfg {
+  static constexpr int DH = DH_;
+  static constexpr int CH = DH / 64;
+  static constexpr int BN = DH <= 128 ? 128 : 64;
+  static constexpr int NT = DH == 64 ? 2 : 1;
+  static constexpr int STAGES = DH == 64 ? 4 : (DH == 128 ? 3 : 2);
+  static constexpr uint32_t kQChunk = kAttnBM * 128;   // 128 rows x 64 halves
+  static constexpr uint32_t kQBytes = CH * kQChunk;    // one query tile
+  static constexpr uint32_t kKVChunk = BN * 128;       // BN rows x 64 halves
+  static constexpr uint32_t kKVBytes = CH * kKVChunk;  // one K (or V) stage
+  static constexpr uint32_t kTileStride = 256;         // TMEM columns between query tiles
+  static constexpr uint32_t kOCol = 0, kSCol = DH, kPCol = DH + BN;
+  static constexpr size_t kSmem = 1024 + (size_t)NT * kQBytes + 2 * (size_t)STAGES * kKVBytes + 512;
+  static_assert(NT == 1 || kPCol + BN / 2 <= kTileStride, "two query tiles must fit in TMEM");
+  static_assert(kPCol + BN / 2 <= kAttnTmemCols, "query tile must fit in TMEM");
+  static_assert(kSmem <= 232448, "shared memory");
+  static_assert(STAGES <= 4, "barrier slots");
+};
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 256 between rescales
 // Of every 8 exponential pairs, this many run as a polynomial on the FMA pipe
 // and the rest on the MUFU unit (which alone would be the softmax bottleneck).
@@ -64,7 +84,7 @@ struct AttnKernelParams {
   const int32_t* q_pos0;
   __half* ctx;
   int ld_ctx;
-  int dh_out;  // real head dim (<= 64): columns of ctx written per head
+  int dh_out;  // real head dim (<= DH): columns of ctx written per head
 };
 
 // Walks the key tiles of one sample in order: segment g, tile i inside it.
@@ -72,12 +92,13 @@ struct AttnKernelParams {
 struct KvWalk {
   const int32_t* off;
   const int32_t* len;
-  int G;
+  int G, bn;
   int g, i, seg_len, seg_off, pos_base;  // pos_base = key position of segment start
-  __device__ void init(const int32_t* o, const int32_t* l, int G_) {
+  __device__ void init(const int32_t* o, const int32_t* l, int G_, int bn_) {
     off = o;
     len = l;
     G = G_;
+    bn = bn_;
     g = 0;
     i = 0;
     pos_base = 0;
@@ -92,13 +113,13 @@ struct KvWalk {
       seg_off = off[g];
     }
   }
-  __device__ int row() const { return seg_off + i * kAttnBN; }
-  __device__ int valid() const { return min(kAttnBN, seg_len - i * kAttnBN); }
-  __device__ int first_pos() const { return pos_base + i * kAttnBN; }
+  __device__ int row() const { return seg_off + i * bn; }
+  __device__ int valid() const { return min(bn, seg_len - i * bn); }
+  __device__ int first_pos() const { return pos_base + i * bn; }
   __device__ void next() {
     if (g >= G) return;
     ++i;
-    if (i * kAttnBN >= seg_len) {
+    if (i * bn >= seg_len) {
       pos_base += seg_len;
       ++g;
       i = 0;
@@ -109,10 +130,10 @@ struct KvWalk {
 
 // Number of key tiles to visit; with causal masking, tiles whose first key is
 // after the last query of the CTA are skipped.
-__device__ __forceinline__ int count_kv_tiles(const int32_t* off, const int32_t* len, int G,
+__device__ __forceinline__ int count_kv_tiles(const int32_t* off, const int32_t* len, int G, int bn,
                                               bool causal, int max_q_pos) {
   KvWalk w;
-  w.init(off, len, G);
+  w.init(off, len, G, bn);
   int t = 0;
   while (w.g < G) {
     if (causal && w.first_pos() > max_q_pos) break;
@@ -131,29 +152,33 @@ constexpr int kRegsLow = 56;
 constexpr int kRegsHigh = 224;
 static_assert(128 * kRegsLow + 256 * kRegsHigh <= kAttnThreads * kLaunchRegs, "register split");
 
+template <int DH>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ,
                              const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const AttnKernelParams p) {
+  using Cfg = AttnCfg<DH>;
+  constexpr int BN = Cfg::BN, CH = Cfg::CH, NT = Cfg::NT, kKVStages = Cfg::STAGES;
+  constexpr uint32_t kQBytes = Cfg::kQBytes, kKVBytes = Cfg::kKVBytes;
   const int h = blockIdx.y, b = blockIdx.z;
   pdl_wait();  // q/k/v and the token plan come from earlier kernels
   const int q_begin = p.q_cu[b];
   const int nq = p.q_cu[b + 1] - q_begin;
-  const int q_tile0 = blockIdx.x * 2;
+  const int q_tile0 = blockIdx.x * NT;
   if (q_tile0 * kAttnBM >= nq) return;  // uniform for the CTA
-  const int ntile = ((q_tile0 + 1) * kAttnBM < nq) ? 2 : 1;
+  const int ntile = (NT == 2 && (q_tile0 + 1) * kAttnBM < nq) ? 2 : 1;
   const int32_t* kv_off = p.kv_off + (int64_t)b * p.kv_len_stride;
   const int32_t* kv_len = p.kv_len + (int64_t)b * p.kv_len_stride;
   const int q_pos0 = (p.causal && p.q_pos0) ? p.q_pos0[b] : 0;
   const int max_q_pos = q_pos0 + min(nq, (q_tile0 + ntile) * kAttnBM) - 1;
-  const int T = count_kv_tiles(kv_off, kv_len, p.G, p.causal != 0, max_q_pos);
+  const int T = count_kv_tiles(kv_off, kv_len, p.G, BN, p.causal != 0, max_q_pos);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
-  uint8_t* sQ = smem;                       // 2 x 16 KB
-  uint8_t* sK = sQ + 2 * kQBytes;           // kKVStages x 16 KB
-  uint8_t* sV = sK + kKVStages * kKVBytes;  // kKVStages x 16 KB
+  uint8_t* sQ = smem;                       // NT query tiles of CH chunks
+  uint8_t* sK = sQ + NT * kQBytes;          // kKVStages x CH chunks of BN rows
+  uint8_t* sV = sK + kKVStages * kKVBytes;  // kKVStages x CH chunks of BN rows
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKVStages * kKVBytes);
   // q_full, k_full[4], v_full[4], k_empty[4], v_empty[4], vfix[4],
   // s_full[2], s_empty[2], p_full[2], pv_done[2], final, exp_done0[4], exp_done1[4]
@@ -225,13 +250,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool q_issued = false;
       if (lane == 0 && !*abort_flag) {
         mbar_arrive_expect_tx(q_full, ntile * kQBytes);
-        tma_load_3d(smem_u32(sQ), &tmQ, q_full, 0, q_begin + q_tile0 * kAttnBM, h);
-        if (ntile == 2)
-          tma_load_3d(smem_u32(sQ + kQBytes), &tmQ, q_full, 0, q_begin + (q_tile0 + 1) * kAttnBM, h);
+        for (int t = 0; t < ntile; ++t)
+          for (int c = 0; c < CH; ++c)
+            tma_load_3d(smem_u32(sQ + t * kQBytes + c * Cfg::kQChunk), &tmQ, q_full, 64 * c,
+                        q_begin + (q_tile0 + t) * kAttnBM, h);
         q_issued = true;
       }
       KvWalk w;
-      w.init(kv_off, kv_len, p.G);
+      w.init(kv_off, kv_len, p.G, BN);
       bool ok = true;
       for (int j = 0; j < T && ok; ++j, w.next()) {
         const int s = j % kKVStages;
@@ -241,27 +267,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           ok = mbar_wait(k_empty(s), ph ^ 1, abort_flag, 200);
           if (ok) {
             mbar_arrive_expect_tx(k_full(s), kKVBytes);
-            tma_load_4d(smem_u32(sK + s * kKVBytes), &tmK, k_full(s), 0, w.row(), h, w.g);
+            for (int c = 0; c < CH; ++c)
+              tma_load_4d(smem_u32(sK + s * kKVBytes + c * Cfg::kKVChunk), &tmK, k_full(s), 64 * c,
+                          w.row(), h, w.g);
             last_k[s] = (int)ph;
             ok = mbar_wait(v_empty(s), ph ^ 1, abort_flag, 201);
           }
           if (ok) {
             mbar_arrive_expect_tx(v_full(s), kKVBytes);
-            tma_load_4d(smem_u32(sV + s * kKVBytes), &tmV, v_full(s), 0, w.row(), h, w.g);
+            for (int c = 0; c < CH; ++c)
+              tma_load_4d(smem_u32(sV + s * kKVBytes + c * Cfg::kKVChunk), &tmV, v_full(s), 64 * c,
+                          w.row(), h, w.g);
             last_v[s] = (int)ph;
           }
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (ok && nvalid < kAttnBN) {
-          // Zero V rows [nvalid, 128) once the tile has landed.
+        if (ok && nvalid < BN) {
+          // Zero V rows [nvalid, BN) of every chunk once the tile has landed.
           ok = mbar_wait(v_full(s), ph, abort_flag, 202);
           ok = __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
           if (ok) {
-            for (int r = nvalid + (int)lane; r < kAttnBN; r += 32) {
-              uint4* vrow = reinterpret_cast<uint4*>(sV + s * kKVBytes + r * 128);
-  #pragma unroll
-              for (int c = 0; c < 8; ++c) vrow[c] = make_uint4(0u, 0u, 0u, 0u);
-            }
+            for (int c = 0; c < CH; ++c)
+              for (int r = nvalid + (int)lane; r < BN; r += 32) {
+                uint4* vrow = reinterpret_cast<uint4*>(sV + s * kKVBytes + c * Cfg::kKVChunk + r * 128);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) vrow[u] = make_uint4(0u, 0u, 0u, 0u);
+              }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(vfix(s));
@@ -288,22 +319,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (warp == 1) {
       // ------------------------------------------------------------ MMA issuer
       if (lane == 0) {
-        constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN, 0, 0);
-        constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, kDH, 0, 1);  // V is MN-major
+        constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, BN, 0, 0);
+        constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, 64, 0, 1);  // one 64-column V chunk, MN-major
         bool issued = false;
         bool ok = mbar_wait(q_full, 0, abort_flag, 210);
         if (ok) tc_fence_after();
-        int nfix[kKVStages] = {0, 0, 0, 0};
+        int nfix[kKVStages];
+        for (int s = 0; s < kKVStages; ++s) nfix[s] = 0;
         // S_t(j) = Q_t K_j^T into the tile's S columns.
-        auto issue_s = [&](int t, int j, uint64_t k_desc) -> bool {
+        auto issue_s = [&](int t, int j, uint32_t k_base) -> bool {
           if (j >= 1 && !mbar_wait(s_empty(t), (uint32_t)((j - 1) & 1), abort_flag, 215)) return false;
           tc_fence_after();
-          const uint64_t q_desc = sw128_desc(smem_u32(sQ + t * kQBytes), 16, 1024);
-          const uint32_t s_tmem = tmem_base + (uint32_t)(t * 256);
+          const uint32_t s_tmem = tmem_base + (uint32_t)(t * Cfg::kTileStride + Cfg::kSCol);
 #pragma unroll
-          for (int k = 0; k < kDH / 16; ++k)
-            mma_f16_ss(s_tmem, q_desc + (uint64_t)(2 * k), k_desc + (uint64_t)(2 * k), idesc_s,
-                       k != 0 ? 1u : 0u);
+          for (int c = 0; c < CH; ++c) {
+            // head-dim chunk c: K=64 of the contraction, 4 x K=16
+            const uint64_t q_desc = sw128_desc(smem_u32(sQ + t * kQBytes + c * Cfg::kQChunk), 16, 1024);
+            const uint64_t k_desc = sw128_desc(k_base + c * Cfg::kKVChunk, 16, 1024);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_f16_ss(s_tmem, q_desc + (uint64_t)(2 * k), k_desc + (uint64_t)(2 * k), idesc_s,
+                         (c | k) != 0 ? 1u : 0u);
+          }
           mma_commit(s_full(t));
           issued = true;
           return true;
@@ -322,13 +359,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!mbar_wait(p_full(t), (uint32_t)(i & 1), abort_flag, 213)) return false;
           tc_fence_after();
           const uint32_t v_base = smem_u32(sV + s * kKVBytes);
-          const uint32_t o_tmem = tmem_base + (uint32_t)(t * 256 + 192);
-          const uint32_t p_tmem = tmem_base + (uint32_t)(t * 256 + 128);
+          const uint32_t o_tmem = tmem_base + (uint32_t)(t * Cfg::kTileStride + Cfg::kOCol);
+          const uint32_t p_tmem = tmem_base + (uint32_t)(t * Cfg::kTileStride + Cfg::kPCol);
 #pragma unroll
-          for (int k = 0; k < kAttnBN / 16; ++k) {
-            // B = V (MN-major): K=16 keys = 16 rows of 128 bytes per step.
-            const uint64_t b_desc = sw128_desc(v_base + (uint32_t)(k * 16 * 128), 1024, 1024);
-            mma_f16_ts(o_tmem, p_tmem + (uint32_t)(k * 8), b_desc, idesc_o, (i | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < BN / 16; ++k) {
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+              // B = V chunk c (MN-major): K=16 keys = 16 rows of 128 bytes per step;
+              // it accumulates into O columns [64c, 64c+64).
+              const uint64_t b_desc =
+                  sw128_desc(v_base + c * Cfg::kKVChunk + (uint32_t)(k * 16 * 128), 1024, 1024);
+              mma_f16_ts(o_tmem + (uint32_t)(64 * c), p_tmem + (uint32_t)(k * 8), b_desc, idesc_o,
+                         (i | k) != 0 ? 1u : 0u);
+            }
           }
           mma_commit(pv_done(t));
           if (t == ntile - 1) mma_commit(v_empty(s));
@@ -342,18 +385,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         auto issue_s_pair = [&](int j) -> bool {
           const int s = j % kKVStages;
           if (!mbar_wait(k_full(s), (uint32_t)((j / kKVStages) & 1), abort_flag, 214)) return false;
-          const uint64_t k_desc = sw128_desc(smem_u32(sK + s * kKVBytes), 16, 1024);
+          const uint32_t k_base = smem_u32(sK + s * kKVBytes);
           for (int t = 0; t < ntile; ++t)
-            if (!issue_s(t, j, k_desc)) return false;
+            if (!issue_s(t, j, k_base)) return false;
           mma_commit(k_empty(s));
           return true;
         };
         KvWalk w;
-        w.init(kv_off, kv_len, p.G);
+        w.init(kv_off, kv_len, p.G, BN);
         if (ok && T > 0) ok = issue_s_pair(0);
         for (int j = 0; ok && j < T; ++j, w.next()) {
           if (j + 1 < T) ok = issue_s_pair(j + 1);
-          const bool boundary = w.valid() < kAttnBN;
+          const bool boundary = w.valid() < BN;
           for (int t = 0; ok && t < ntile; ++t) ok = issue_pv(t, j, boundary);
         }
         if (issued) {
@@ -371,8 +414,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + (int)lane;
     if (t < ntile) {
-      const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * 256);
-      const uint32_t s_tmem = t_lane, p_tmem = t_lane + 128u, o_tmem = t_lane + 192u;
+      const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(t * Cfg::kTileStride);
+      const uint32_t s_tmem = t_lane + Cfg::kSCol, p_tmem = t_lane + Cfg::kPCol, o_tmem = t_lane + Cfg::kOCol;
       const float sl2 = p.scale_log2;
       const int q_local = (q_tile0 + t) * kAttnBM + row;
       const int q_pos = q_pos0 + q_local;
@@ -381,18 +424,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
 
       KvWalk w;
-      w.init(kv_off, kv_len, p.G);
+      w.init(kv_off, kv_len, p.G, BN);
       for (int j = 0; j < T; ++j, w.next()) {
         if (!mbar_wait(s_full(t), (uint32_t)(j & 1), abort_flag, 220)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sr[kAttnBN];
-        tmem_ld32(s_tmem + 0u, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
-        tmem_ld32(s_tmem + 32u, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-        tmem_ld32(s_tmem + 64u, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-        tmem_ld32(s_tmem + 96u, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+        uint32_t sr[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_ld32(s_tmem + (uint32_t)(32 * c), *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c));
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
@@ -402,21 +444,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // the keys after this query.
         int lim = w.valid();
         if (p.causal) lim = min(lim, q_pos - w.first_pos() + 1);
-        if (lim < kAttnBN) {
+        if (lim < BN) {
 #pragma unroll
-          for (int c = 0; c < kAttnBN; ++c)
+          for (int c = 0; c < BN; ++c)
             if (c >= lim) sr[c] = __float_as_uint(-INFINITY);
         }
         float pm[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) pm[u] = __uint_as_float(sr[u]);
 #pragma unroll
-        for (int c = 8; c < kAttnBN - 8; c += 16)
+        for (int c = 8; c < BN - 8; c += 16)
 #pragma unroll
           for (int u = 0; u < 8; ++u)
             pm[u] = fmax3(pm[u], __uint_as_float(sr[c + u]), __uint_as_float(sr[c + 8 + u]));
 #pragma unroll
-        for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], __uint_as_float(sr[kAttnBN - 8 + u]));
+        for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], __uint_as_float(sr[BN - 8 + u]));
         const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                                fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
         const float m_cand = fmaxf(m_run, mx * sl2);
@@ -449,9 +491,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         // P is computed into registers first, so the exponentials overlap the
         // tensor core's P_{j-1} V_{j-1}; only the TMEM stores wait for it.
-        uint32_t pk[64];
+        uint32_t pk[BN / 2];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < BN / 2; ++c) {
           float2 x = ffma2(make_float2(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])), sl2v, negm);
           if ((c & 7) < kPolyPairsPer8) {
             x = exp2_poly2(x);  // FMA pipe
@@ -475,21 +517,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tc_fence_after();
           if (need) {
-            uint32_t o[32];
-            tmem_ld32(o_tmem, o);
-            tmem_ld_wait();
+#pragma unroll 1
+            for (int c = 0; c < DH / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(o_tmem + (uint32_t)(32 * c), o);
+              tmem_ld_wait();
 #pragma unroll
-            for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
-            tmem_st32(o_tmem, o);
-            tmem_ld32(o_tmem + 32u, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
-            tmem_st32(o_tmem + 32u, o);
+              for (int d = 0; d < 32; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+              tmem_st32(o_tmem + (uint32_t)(32 * c), o);
+            }
           }
         }
-        tmem_st32(p_tmem, *reinterpret_cast<uint32_t(*)[32]>(pk + 0));
-        tmem_st32(p_tmem + 32u, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+          tmem_st32(p_tmem + (uint32_t)(32 * c), *reinterpret_cast<uint32_t(*)[32]>(pk + 32 * c));
         tmem_st_wait();
         const float2 a01 = fadd2(acc[0], acc[1]), a23 = fadd2(acc[2], acc[3]);
         const float2 a = fadd2(a01, a23);
@@ -503,45 +544,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (ok) tc_fence_after();
       }
       ok = __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
-      if (ok) {
+      if (ok) {  // warp-uniform: the TMEM loads below are warp-collective
         const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-        uint32_t o0[32], o1[32];
-        if (T > 0) {
-          tmem_ld32(o_tmem, o0);
-          tmem_ld32(o_tmem + 32u, o1);
-          tmem_ld_wait();
-        } else {
+        __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * p.dh_out;
+#pragma unroll 1
+        for (int c = 0; c < DH / 32; ++c) {
+          if (32 * c >= p.dh_out) break;
+          uint32_t o[32];
+          if (T > 0) {
+            tmem_ld32(o_tmem + (uint32_t)(32 * c), o);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-          for (int d = 0; d < 32; ++d) o0[d] = o1[d] = 0u;
-        }
-        if (q_local < nq && p.dh_out != kDH) {
-          // Head dim below 64: the padded columns are dropped.
-          __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * p.dh_out;
-#pragma unroll
-          for (int d = 0; d < 32; ++d)
-            if (d < p.dh_out) dst[d] = __float2half_rn(__uint_as_float(o0[d]) * inv_l);
-#pragma unroll
-          for (int d = 0; d < 32; ++d)
-            if (32 + d < p.dh_out) dst[32 + d] = __float2half_rn(__uint_as_float(o1[d]) * inv_l);
-        } else if (q_local < nq) {
-          __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * kDH;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint4 v;
-            v.x = pack_half2(__uint_as_float(o0[8 * c + 0]) * inv_l, __uint_as_float(o0[8 * c + 1]) * inv_l);
-            v.y = pack_half2(__uint_as_float(o0[8 * c + 2]) * inv_l, __uint_as_float(o0[8 * c + 3]) * inv_l);
-            v.z = pack_half2(__uint_as_float(o0[8 * c + 4]) * inv_l, __uint_as_float(o0[8 * c + 5]) * inv_l);
-            v.w = pack_half2(__uint_as_float(o0[8 * c + 6]) * inv_l, __uint_as_float(o0[8 * c + 7]) * inv_l);
-            reinterpret_cast<uint4*>(dst)[c] = v;
+            for (int d = 0; d < 32; ++d) o[d] = 0u;
           }
+          if (q_local >= nq) continue;
+          if ((p.dh_out & 7) == 0 && 32 * c + 32 <= p.dh_out) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint4 v;
-            v.x = pack_half2(__uint_as_float(o1[8 * c + 0]) * inv_l, __uint_as_float(o1[8 * c + 1]) * inv_l);
-            v.y = pack_half2(__uint_as_float(o1[8 * c + 2]) * inv_l, __uint_as_float(o1[8 * c + 3]) * inv_l);
-            v.z = pack_half2(__uint_as_float(o1[8 * c + 4]) * inv_l, __uint_as_float(o1[8 * c + 5]) * inv_l);
-            v.w = pack_half2(__uint_as_float(o1[8 * c + 6]) * inv_l, __uint_as_float(o1[8 * c + 7]) * inv_l);
-            reinterpret_cast<uint4*>(dst)[4 + c] = v;
+            for (int g = 0; g < 4; ++g) {
+              uint4 v;
+              v.x = pack_half2(__uint_as_float(o[8 * g + 0]) * inv_l, __uint_as_float(o[8 * g + 1]) * inv_l);
+              v.y = pack_half2(__uint_as_float(o[8 * g + 2]) * inv_l, __uint_as_float(o[8 * g + 3]) * inv_l);
+              v.z = pack_half2(__uint_as_float(o[8 * g + 4]) * inv_l, __uint_as_float(o[8 * g + 5]) * inv_l);
+              v.w = pack_half2(__uint_as_float(o[8 * g + 6]) * inv_l, __uint_as_float(o[8 * g + 7]) * inv_l);
+              reinterpret_cast<uint4*>(dst + 32 * c)[g] = v;
+            }
+          } else {
+            // Head dims that are not a multiple of 32 (or of 8): the padded
+            // columns are dropped.
+#pragma unroll
+            for (int d = 0; d < 32; ++d)
+              if (32 * c + d < p.dh_out) dst[32 * c + d] = __float2half_rn(__uint_as_float(o[d]) * inv_l);
           }
         }
       }
@@ -557,34 +590,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
-int launch_attention(const AttnArgs& a, cudaStream_t stream) {
-  if (a.head_dim <= 0 || a.head_dim > kDH)
-    return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: head_dim %d (1..64 supported)", a.head_dim);
-  if (a.H <= 0 || a.B <= 0 || a.G <= 0 || a.q_rows < 0 || a.kv_rows < 0 || a.max_q_per_sample < 0)
-    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: bad sizes H=%d B=%d G=%d", a.H, a.B, a.G);
-  if (!a.q || !a.k || !a.v || !a.ctx || !a.q_cu || !a.kv_off || !a.kv_len)
-    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: null pointer");
-  if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
-       reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.ctx)) & 15u)
-    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: operands must be 16-byte aligned");
-  if (a.kv_stride_h % 8 != 0 || a.kv_stride_g % 8 != 0)
-    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: K/V strides must be multiples of 8 elements");
-  if (a.causal && a.G > 1 && a.q_pos0 == nullptr)
-    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: causal with key segments needs q_pos0");
-  if (a.q_rows == 0 || a.max_q_per_sample == 0 || a.kv_rows == 0) return TJ_OK;
+// Row length (halves) of the q/k/v buffers for a head dim: heads are
+// zero-padded to 64, 128 or 256.
+int attn_head_pad(int head_dim) { return head_dim <= 64 ? 64 : (head_dim <= 128 ? 128 : 256); }
 
+template <int DH>
+static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
+  using Cfg = AttnCfg<DH>;
   CUtensorMap tq, tk, tv;
   {
-    uint64_t d[3] = {(uint64_t)kDH, (uint64_t)a.q_rows, (uint64_t)a.H};
-    uint64_t s[2] = {(uint64_t)kDH, (uint64_t)kDH * a.q_rows};
-    uint32_t bx[3] = {kDH, kAttnBM, 1};
+    uint64_t d[3] = {(uint64_t)DH, (uint64_t)a.q_rows, (uint64_t)a.H};
+    uint64_t s[2] = {(uint64_t)DH, (uint64_t)DH * a.q_rows};
+    uint32_t bx[3] = {64, kAttnBM, 1};
     int rc = make_tmap_f16(&tq, a.q, 3, d, s, bx);
     if (rc) return rc;
   }
   {
-    uint64_t d[4] = {(uint64_t)kDH, (uint64_t)a.kv_rows, (uint64_t)a.H, (uint64_t)a.G};
-    uint64_t s[3] = {(uint64_t)kDH, (uint64_t)a.kv_stride_h, (uint64_t)a.kv_stride_g};
-    uint32_t bx[4] = {kDH, kAttnBN, 1, 1};
+    uint64_t d[4] = {(uint64_t)DH, (uint64_t)a.kv_rows, (uint64_t)a.H, (uint64_t)a.G};
+    uint64_t s[3] = {(uint64_t)DH, (uint64_t)a.kv_stride_h, (uint64_t)a.kv_stride_g};
+    uint32_t bx[4] = {64, (uint32_t)Cfg::BN, 1, 1};
     int rc = make_tmap_f16(&tk, a.k, 4, d, s, bx);
     if (rc) return rc;
     rc = make_tmap_f16(&tv, a.v, 4, d, s, bx);
@@ -599,16 +623,16 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   const int dev = device_index();
   if (!attr_set[dev]) {
     cudaFuncAttributes fa;
-    cudaError_t e0 = cudaFuncGetAttributes(&fa, attention_tcgen05_kernel);
+    cudaError_t e0 = cudaFuncGetAttributes(&fa, attention_tcgen05_kernel<DH>);
     if (e0 != cudaSuccess)
       return set_error(TJ_ERR_CUDA, "attention attributes: %s", cudaGetErrorString(e0));
     if (fa.numRegs != kLaunchRegs)
       return set_error(TJ_ERR_UNSUPPORTED,
-                       "attention kernel built with %d registers per thread, the register split "
-                       "assumes %d; refusing to launch",
-                       fa.numRegs, kLaunchRegs);
-    cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem);
+                       "attention kernel (head dim %d) built with %d registers per thread, the "
+                       "register split assumes %d; refusing to launch",
+                       DH, fa.numRegs, kLaunchRegs);
+    cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel<DH>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
     if (e != cudaSuccess)
       return set_error(TJ_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev] = true;
@@ -627,14 +651,40 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   kp.ctx = static_cast<__half*>(a.ctx);
   kp.ld_ctx = a.H * a.head_dim;
   kp.dh_out = a.head_dim;
-  dim3 grid((a.max_q_per_sample + 2 * kAttnBM - 1) / (2 * kAttnBM), a.H, a.B);
+  constexpr int kQPerCta = Cfg::NT * kAttnBM;
+  dim3 grid((a.max_q_per_sample + kQPerCta - 1) / kQPerCta, a.H, a.B);
   if (grid.y > 65535 || grid.z > 65535)
     return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d or B=%d above 65535", a.H, a.B);
-  cudaError_t e = launch_pdl(attention_tcgen05_kernel, grid, dim3(kAttnThreads), kAttnSmem, stream, tq,
-                             tk, tv, kp);
+  cudaError_t e = launch_pdl(attention_tcgen05_kernel<DH>, grid, dim3(kAttnThreads), Cfg::kSmem, stream,
+                             tq, tk, tv, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
   return TJ_OK;
+}
+
+int launch_attention(const AttnArgs& a, cudaStream_t stream) {
+  if (a.head_dim <= 0 || a.head_dim > 256)
+    return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: head_dim %d (1..256 supported)", a.head_dim);
+  if (a.H <= 0 || a.B <= 0 || a.G <= 0 || a.q_rows < 0 || a.kv_rows < 0 || a.max_q_per_sample < 0)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: bad sizes H=%d B=%d G=%d", a.H, a.B, a.G);
+  if (!a.q || !a.k || !a.v || !a.ctx || !a.q_cu || !a.kv_off || !a.kv_len)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: null pointer");
+  if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+       reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.ctx)) & 15u)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: operands must be 16-byte aligned");
+  if (a.kv_stride_h % 8 != 0 || a.kv_stride_g % 8 != 0)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: K/V strides must be multiples of 8 elements");
+  if (a.causal && a.G > 1 && a.q_pos0 == nullptr)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: causal with key segments needs q_pos0");
+  if (a.q_rows == 0 || a.max_q_per_sample == 0 || a.kv_rows == 0) return TJ_OK;
+  switch (attn_head_pad(a.head_dim)) {
+    case 64:
+      return launch_attention_t<64>(a, stream);
+    case 128:
+      return launch_attention_t<128>(a, stream);
+    default:
+      return launch_attention_t<256>(a, stream);
+  }
 }
 
 }  // namespace tj

@@ -44,7 +44,6 @@ __host__ __device__ constexpr int gemm_threads_for(int bn, int epi) {
 }
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kHeadPad = 64;  // head-major row length (halves) of the QKV output
 
 struct GemmKernelParams {
   const float* bias;
@@ -56,6 +55,7 @@ struct GemmKernelParams {
   const int32_t* resid_map;
   int ld_resid;
   int heads, head_dim, d_model;
+  int head_pad;  // head-major row length (halves) of the QKV output: 64, 128 or 256
 };
 
 // Shared-memory scratch of the epilogue warps (one 32-row block each), used to
@@ -255,10 +255,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
               const int rem = n - which * p.d_model;
               const int h = rem / p.head_dim;
               const int d = rem - h * p.head_dim;
-              __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
+              __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * p.head_pad;
               *reinterpret_cast<uint4*>(rowp + d) = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
               if (d + 8 == p.head_dim)
-                for (int z = p.head_dim; z < kHeadPad; z += 8)
+                for (int z = p.head_dim; z < p.head_pad; z += 8)
                   *reinterpret_cast<uint4*>(rowp + z) = make_uint4(0u, 0u, 0u, 0u);
             } else {
 #pragma unroll
@@ -268,11 +268,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
                 const int rem = ne - which * p.d_model;
                 const int h = rem / p.head_dim;
                 const int d = rem - h * p.head_dim;
-                __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * kHeadPad;
+                __half* rowp = qkv + ((int64_t)(which * p.heads + h) * p.rows_max + row) * p.head_pad;
                 const uint32_t bits = pk[4 * g + (e >> 1)] >> ((e & 1) * 16);
                 rowp[d] = __ushort_as_half((unsigned short)(bits & 0xFFFFu));
                 if (d + 1 == p.head_dim)
-                  for (int z = p.head_dim; z < kHeadPad; ++z) rowp[z] = __float2half_rn(0.f);
+                  for (int z = p.head_dim; z < p.head_pad; ++z) rowp[z] = __float2half_rn(0.f);
               }
             }
           }
@@ -296,16 +296,18 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
         if (EPI != kEpiQkvHeadMajor) {
           *reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + (int64_t)orow * p.ld_out + col) = v;
         } else {
-          // A 32-column chunk lies inside one head (head_dim is 32 or 64).
+          // A 32-column chunk lies inside one head (head_dim is a multiple of 32);
+          // the writer of a head's last chunk zeroes its padding up to head_pad.
           const int which = nc / p.d_model;
           const int rem = nc - which * p.d_model;
           const int h = rem / p.head_dim;
           const int d0 = rem - h * p.head_dim;
           __half* rowp = static_cast<__half*>(p.out) +
-                         ((int64_t)(which * p.heads + h) * p.rows_max + orow) * kHeadPad;
+                         ((int64_t)(which * p.heads + h) * p.rows_max + orow) * p.head_pad;
           *reinterpret_cast<uint4*>(rowp + d0 + 8 * (int)k) = v;
-          if (p.head_dim == 32)
-            *reinterpret_cast<uint4*>(rowp + 32 + 8 * (int)k) = make_uint4(0u, 0u, 0u, 0u);
+          if (d0 + 32 == p.head_dim)
+            for (int z = p.head_dim + 8 * (int)k; z < p.head_pad; z += 32)
+              *reinterpret_cast<uint4*>(rowp + z) = make_uint4(0u, 0u, 0u, 0u);
         }
       }
       __syncwarp();  // the next chunk reuses the scratch
@@ -862,11 +864,12 @@ int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
   kp.head_dim = a.head_dim;
   switch (epilogue) {
     case kEpiQkvHeadMajor:
-      if (a.heads <= 0 || a.head_dim <= 0 || a.head_dim > kHeadPad || a.N != 3 * a.heads * a.head_dim)
+      if (a.heads <= 0 || a.head_dim <= 0 || a.head_dim > 256 || a.N != 3 * a.heads * a.head_dim)
         return set_error(TJ_ERR_UNSUPPORTED,
-                         "gemm_qkv_headmajor: N=%d must be 3*H*dh with dh <= %d (H=%d dh=%d)",
-                         a.N, kHeadPad, a.heads, a.head_dim);
+                         "gemm_qkv_headmajor: N=%d must be 3*H*dh with dh <= 256 (H=%d dh=%d)",
+                         a.N, a.heads, a.head_dim);
       kp.d_model = a.heads * a.head_dim;
+      kp.head_pad = attn_head_pad(a.head_dim);
       return launch_gemm_bn<kEpiQkvHeadMajor>(a, kp, stream);
     case kEpiResidualF32:
       if (!a.resid || (reinterpret_cast<uintptr_t>(a.resid) & 15u) || a.ld_resid % 4 != 0 ||

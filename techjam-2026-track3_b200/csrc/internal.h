@@ -73,7 +73,7 @@ int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, con
                     const void* add16 = nullptr);
 
 enum GemmEpilogue : int {
-  kEpiQkvHeadMajor = 0,   // fp16 out, head-major [3][H][rows_max][dh]
+  kEpiQkvHeadMajor = 0,   // fp16 out, head-major [3][H][rows_max][attn_head_pad(dh)]
   kEpiResidualF32 = 1,    // fp32 out = acc + bias + residual[row_map(row)]
   kEpiGeluF16 = 2,        // fp16 out = gelu_erf(acc + bias)
   kEpiBiasF16 = 3,        // fp16 out = acc + bias
@@ -96,8 +96,8 @@ struct GemmArgs {
 int launch_gemm(int epilogue, const GemmArgs& args, cudaStream_t stream);
 
 struct AttnArgs {
-  const void* q;            // fp16 [H][q_rows][dh]
-  const void* k;            // fp16, addressed as [G][H][kv_rows][dh] with strides below
+  const void* q;            // fp16 [H][q_rows][P], P = attn_head_pad(head_dim)
+  const void* k;            // fp16, addressed as [G][H][kv_rows][P] with strides below
   const void* v;
   int H, head_dim;
   int q_rows;               // rows of the Q slab per head
@@ -118,5 +118,9 @@ struct AttnArgs {
 };
 
 int launch_attention(const AttnArgs& args, cudaStream_t stream);
+
+// Row length (halves) of the head-major q/k/v buffers for a head dim: 64,
+// 128 or 256 (heads are zero-padded up to it).
+int attn_head_pad(int head_dim);
 
 }  // namespace tj

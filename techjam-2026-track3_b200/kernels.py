@@ -25,6 +25,14 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def head_pad(head_dim: int) -> int:
+    """Row length (halves) of the head-major q/k/v buffers: heads are
+    zero-padded to 64, 128 or 256."""
+    if not 1 <= head_dim <= 256:
+        raise ValueError(f"head_dim must be in 1..256, got {head_dim}")
+    return 64 if head_dim <= 64 else (128 if head_dim <= 128 else 256)
+
+
 def _require(t: torch.Tensor, name: str, dtype: torch.dtype, device: torch.device) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a tensor")
@@ -168,9 +176,9 @@ def gemm_qkv_headmajor(a16, w_qkv16, b_qkv, num_heads, row_count=None, out=None)
     if w_qkv16.shape != (3 * D, D):
         raise ValueError(f"w_qkv16 must be [{3 * D}, {D}], got {tuple(w_qkv16.shape)}")
     if out is None:
-        # head-major, each head zero-padded to 64 halves
-        out = torch.empty(3, num_heads, rows, 64, dtype=torch.float16, device=dev)
-    _require_out(out, "out", (3, num_heads, rows, 64), torch.float16, dev)
+        # head-major, each head zero-padded to head_pad(D // H) halves
+        out = torch.empty(3, num_heads, rows, head_pad(D // num_heads), dtype=torch.float16, device=dev)
+    _require_out(out, "out", (3, num_heads, rows, head_pad(D // num_heads)), torch.float16, dev)
     lib = _lib.load()
     rc = lib.tj_gemm_qkv_headmajor(
         a16.data_ptr(), w_qkv16.data_ptr(), b_qkv.data_ptr(), _ptr(row_count), rows, D, num_heads,
@@ -253,8 +261,9 @@ def gemm_bias_gelu_f16(a16, w16, bias, row_count=None, out=None):
 
 def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causal=False,
                    q_pos0=None, out=None, head_dim=64):
-    """q: [H, q_rows, 64]; k, v: [G, H, kv_rows, 64] (any strides with unit inner stride;
-    rows hold head_dim values then zeros up to 64); q_cu: [B+1]; kv_off/kv_len: [B, G]
+    """q: [H, q_rows, P]; k, v: [G, H, kv_rows, P] with P = head_pad(head_dim) (any strides
+    with unit inner stride; rows hold head_dim values then zeros up to P); q_cu: [B+1];
+    kv_off/kv_len: [B, G]
     int32.  Returns ctx [q_rows, H*head_dim] fp16."""
     dev = q.device
     _require(q, "q", torch.float16, dev)
@@ -262,13 +271,12 @@ def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causa
         k = k.unsqueeze(0)
         v = v.unsqueeze(0)
     G, H, kv_rows, row = k.shape
-    if row != 64 or q.shape[0] != H or q.shape[2] != 64:
-        raise ValueError("q, k, v rows must be 64 halves (head dims below 64 zero-padded)")
-    if k.stride() != v.stride() or k.stride(-1) != 1 or k.stride(-2) != 64:
-        raise ValueError("k and v must share strides with contiguous [rows, 64] slabs")
     dh = head_dim
-    if not 1 <= dh <= 64:
-        raise ValueError(f"head_dim must be in 1..64, got {dh}")
+    P = head_pad(dh)
+    if row != P or q.shape[0] != H or q.shape[2] != P:
+        raise ValueError(f"q, k, v rows must be {P} halves (head dim {dh} zero-padded)")
+    if k.stride() != v.stride() or k.stride(-1) != 1 or k.stride(-2) != P:
+        raise ValueError(f"k and v must share strides with contiguous [rows, {P}] slabs")
     B = q_cu.numel() - 1
     if out is None:
         out = torch.empty(q.shape[1], H * dh, dtype=torch.float16, device=dev)

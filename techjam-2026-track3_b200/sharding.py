@@ -11,7 +11,7 @@ One process per GPU (torchrun), torch.distributed for the plumbing.
 * Context parallelism for one long sequence: rank g holds a contiguous chunk
   of the sequence.  Attention is the only op that mixes tokens, so each rank
   computes LN1 and the QKV projection for its own tokens, all-gathers the
-  K/V slabs with NCCL (all_gather_into_tensor into [G][2][H][slab][64], which
+  K/V slabs with NCCL (all_gather_into_tensor into [G][2][H][slab][P], which
   the attention kernel reads as G key segments), runs attention for its own
   queries over every segment, and the rest of the layer is token-local.
 
@@ -147,8 +147,9 @@ class ContextParallelEncoder:
         kv_off, kv_len, q_pos0 = segment_metadata(counts, self.rank, bool(cfg.causal))
 
         a16 = torch.empty(slab, D, dtype=torch.float16, device=dev)
-        qkv = torch.empty(3, H, slab, 64, dtype=torch.float16, device=dev)  # heads padded to 64
-        kv_all = torch.empty(self.world, 2, H, slab, 64, dtype=torch.float16, device=dev)
+        P = kernels.head_pad(dh)  # heads zero-padded to P halves
+        qkv = torch.empty(3, H, slab, P, dtype=torch.float16, device=dev)
+        kv_all = torch.empty(self.world, 2, H, slab, P, dtype=torch.float16, device=dev)
         ctx = torch.empty(slab, D, dtype=torch.float16, device=dev)
         h16 = torch.empty(slab, F, dtype=torch.float16, device=dev)
         y16 = torch.empty(Sl, D, dtype=torch.float16, device=dev)

@@ -129,17 +129,20 @@ def _gemm_ref(a16, w16, bias):
     [(128, 128, 256, 4), (1000, 777, 768, 12), (4096, 4096, 1024, 16), (300, 0, 256, 4),
      (200, 150, 256, 8), (40, 33, 16, 4), (77, 77, 96, 4),
      # CTA-pair tiles (256 rows): second CTA partly valid / without valid rows / past rows_max
-     (5000, 4321, 768, 12), (5000, 4196, 768, 12), (4100, 4100, 768, 12)],
+     (5000, 4321, 768, 12), (5000, 4196, 768, 12), (4100, 4100, 768, 12),
+     # head dims above 64: rows padded to 128 / 256 halves
+     (500, 480, 256, 2), (300, 300, 512, 2), (200, 190, 192, 2), (100, 100, 320, 2), (64, 64, 144, 2)],
 )
 def test_gemm_qkv_headmajor(cuda_pkg, rows, count, D, H):
-    """Head-major output [3][H][rows][64]; head dims below 64 zero-padded."""
+    """Head-major output [3][H][rows][P]; head dims below P (64/128/256) zero-padded."""
     k = cuda_pkg.kernels
     dh = D // H
+    P = k.head_pad(dh)
     g = torch.Generator().manual_seed(rows + D)
     a = torch.randn(rows, D, generator=g).half().to(DEV)
     w = (torch.randn(3 * D, D, generator=g) / math.sqrt(D)).half().to(DEV)
     b = torch.randn(3 * D, generator=g).to(DEV)
-    out = torch.full((3, H, rows, 64), float("nan"), dtype=torch.float16, device=DEV)
+    out = torch.full((3, H, rows, P), float("nan"), dtype=torch.float16, device=DEV)
     k.gemm_qkv_headmajor(a, w, b, H, row_count=torch.tensor([count], dtype=torch.int32, device=DEV), out=out)
     ref = _gemm_ref(a, w, b)  # [rows, 3D]
     ref_hm = ref.view(rows, 3, H, dh).permute(1, 2, 0, 3)
@@ -147,7 +150,7 @@ def test_gemm_qkv_headmajor(cuda_pkg, rows, count, D, H):
     exp = ref_hm[:, :, :count]
     # fp32 accumulation of fp16 products, then one fp16 rounding.
     assert torch.all((got - exp).abs() <= exp.abs() * 2**-10 + 2e-3), float((got - exp).abs().max())
-    if dh < 64:
+    if dh < P:
         assert torch.count_nonzero(out[:, :, :count, dh:].float()) == 0, "head padding must be zero"
     if count < rows:
         assert torch.isnan(out[:, :, count:].float()).all(), "rows past the count must not be written"
@@ -201,7 +204,7 @@ def test_gemm_bias_f16(cuda_pkg, rows, count, N, K):
 
 
 def _attn_ref(q, k, v, q_cu, kv_off, kv_len, scale, causal=False, dh=64):
-    """q [H, rows, 64] fp16; k/v [G, H, rows, 64]; fp32 math per sample."""
+    """q [H, rows, P] fp16; k/v [G, H, rows, P]; fp32 math per sample."""
     H = q.shape[0]
     q, k, v = q[..., :dh], k[..., :dh], v[..., :dh]
     out = torch.zeros(q.shape[1], H * dh, dtype=torch.float32, device=q.device)
@@ -291,3 +294,31 @@ def test_flash_attention_small_heads(cuda_pkg, dh):
     assert out.shape == (400, H * dh)
     ref = _attn_ref(qkv[0], qkv[1:2], qkv[2:3], cu, kv_off, kv_len, scale, dh=dh)
     assert float((out[:377].float() - ref[:377]).abs().max()) < 4e-3
+
+
+@pytest.mark.parametrize("dh,H", [(128, 2), (96, 3), (256, 2), (160, 1)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_attention_large_heads(cuda_pkg, dh, H, causal):
+    """Head dims above 64: rows zero-padded to 128 or 256 halves (one query tile
+    per CTA; 64-key tiles at head dim 256), ragged and empty samples."""
+    k = cuda_pkg.kernels
+    P = k.head_pad(dh)
+    g = torch.Generator().manual_seed(dh * 10 + H + int(causal))
+    lengths = [300, 1, 0, 129, 700]
+    lens = torch.tensor(lengths, dtype=torch.int32)
+    cu = torch.zeros(len(lengths) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    n = int(cu[-1])
+    rows = n + 64
+    qkv = torch.zeros(3, H, rows, P, dtype=torch.float16)
+    qkv[..., :dh] = torch.randn(3, H, rows, dh, generator=g).half()
+    qkv[:, :, n:] = float("nan")  # slack rows must never leak in
+    qkv = qkv.to(DEV)
+    kv_off, kv_len = cu[:-1].view(-1, 1).contiguous(), lens.view(-1, 1).contiguous()
+    scale = dh**-0.5
+    out = k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu.to(DEV), kv_off.to(DEV), kv_len.to(DEV),
+                           max(lengths), scale, causal=causal, head_dim=dh)
+    assert out.shape == (rows, H * dh)
+    ref = _attn_ref(qkv[0], qkv[1:2], qkv[2:3], cu, kv_off, kv_len, scale, causal=causal, dh=dh)
+    assert torch.isfinite(out[:n].float()).all()
+    assert float((out[:n].float() - ref[:n]).abs().max()) < 4e-3

@@ -137,6 +137,17 @@ def test_no_mask_all_padded_and_determinism(cuda_pkg):
     assert torch.count_nonzero(out[1]) == 0
 
 
+@pytest.mark.parametrize("cfg_t,pad", [((2, 512, 256, 2, 1024, 1, False), 0.3),   # head dim 128
+                                       ((2, 384, 512, 2, 1024, 2, True), 0.2),    # head dim 256, causal
+                                       ((3, 200, 288, 3, 576, 1, False), 0.4)])   # head dim 96
+def test_large_head_dims(cuda_pkg, cfg_t, pad):
+    cfg = oracle.TransformerConfig(*cfg_t)
+    sd = oracle.make_state_dict(cfg, seed=17)
+    x, mask = oracle.generate_random_case(cfg, seed=17, padding_ratio=pad)
+    out = _run(_model(cuda_pkg, cfg, sd), x, mask)
+    _gate(oracle.encoder_forward(sd, cfg, x, mask), out, f"{cfg_t}")
+
+
 def test_two_layers_causal(cuda_pkg):
     cfg = oracle.TransformerConfig(2, 640, 256, 4, 1024, 2, True)
     sd = oracle.make_state_dict(cfg, seed=21)
