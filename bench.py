@@ -285,11 +285,6 @@ def run_ours(args, world, rank, local):
 
     if args.workload == "long" and world > 1:
         return run_context_parallel(args, world, rank, local)
-    B_, S_, D_, H_ = WORKLOADS[args.workload][:4]
-    if D_ // H_ > 64:
-        return None if rank else {"metric": "layer-forward tokens/s", "impl": "ours",
-                                  "config": {"workload": WORKLOADS[args.workload][-1]},
-                                  "unsupported": f"head_dim {D_ // H_} (this build supports 1..64)"}
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     init_dist(world, "nccl")
@@ -477,7 +472,7 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
     nv = int(nv_t.item())
     lens = cnt.double().cpu()
     a16 = torch.empty(rows, D, dtype=torch.float16, device=device)
-    qkv = torch.empty(3, H, rows, 64, dtype=torch.float16, device=device)
+    qkv = torch.empty(3, H, rows, k.head_pad(dh), dtype=torch.float16, device=device)
     ctx = torch.empty(rows, D, dtype=torch.float16, device=device)
     x1 = torch.empty(rows, D, dtype=torch.float32, device=device)
     h16 = torch.empty(rows, F, dtype=torch.float16, device=device)
