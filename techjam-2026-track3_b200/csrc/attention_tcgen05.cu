@@ -36,9 +36,7 @@ namespace tj {
 int make_tmap_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                   const uint64_t* strides_elems, const uint32_t* box);
 
-constexpr int kAttnThreads = 384;
 constexpr int kAttnBM = 128;     // queries per tile
-constexpr uint32_t kAttnTmemCols = 512;
 
 // Per padded head dim DH (the q/k/v row length: 64, 128 or 256; head dims
 // below it are zero-padded): 64-column chunks CH (one 128-byte swizzle atom
@@ -46,13 +44,29 @@ constexpr uint32_t kAttnTmemCols = 512;
 // chosen so shared memory (<= 227 KB) and TMEM (512 columns) hold them.
 // TMEM per query tile: O [0, DH), S [DH, DH+BN), P [DH+BN, DH+BN+BN/2) (fp16
 // pairs); DH=64 packs two tiles at a 256-column stride.
-template <int DH_>
+// SHORT (DH=64, at most 128 queries per sample): one query tile, two stages,
+// 256 threads and 256 TMEM columns, so two CTAs share an SM and one CTA's
+// pipeline fill and drain overlap the other's work -- short sequences have a
+// single key tile per (sample, head), so that latency is most of a CTA's life.
+template <int DH_, bool SHORT = false>
 struct AttnCfg {
   static constexpr int DH = DH_;
   static constexpr int CH = DH / 64;
   static constexpr int BN = DH <= 128 ? 128 : 64;
-  static constexpr int NT = DH == 64 ? 2 : 1;
-  static constexpr int STAGES = DH == 64 ? 4 : (DH == 128 ? 3 : 2);
+  static constexpr int NT = (DH == 64 && !SHORT) ? 2 : 1;
+  static constexpr int STAGES = SHORT ? 2 : (DH == 64 ? 4 : (DH == 128 ? 3 : 2));
+  static constexpr int kThreads = SHORT ? 256 : 384;
+  static constexpr int kMinBlocks = SHORT ? 2 : 1;
+  static constexpr uint32_t kTmemCols = SHORT ? 256 : 512;
+  // Register split: the producer/MMA warpgroup gives registers to the softmax
+  // warpgroup(s).  kLaunchRegs is what ptxas must allocate (the launcher checks
+  // the built kernel); 128*kRegsLow + (kThreads-128)*kRegsHigh may not exceed
+  // kThreads*kLaunchRegs or setmaxnreg.inc would wait forever.
+  static constexpr int kLaunchRegs = SHORT ? 128 : 168;
+  static constexpr int kRegsLow = 56;
+  static constexpr int kRegsHigh = SHORT ? 200 : 224;
+  static_assert(128 * kRegsLow + (kThreads - 128) * kRegsHigh <= kThreads * kLaunchRegs, "register split");
+  static_assert(kThreads * kLaunchRegs * kMinBlocks <= 65536, "register file");
   static constexpr uint32_t kQChunk = kAttnBM * 128;   // 128 rows x 64 halves
   static constexpr uint32_t kQBytes = CH * kQChunk;    // one query tile
   static constexpr uint32_t kKVChunk = BN * 128;       // BN rows x 64 halves
@@ -61,8 +75,8 @@ struct AttnCfg {
   static constexpr uint32_t kOCol = 0, kSCol = DH, kPCol = DH + BN;
   static constexpr size_t kSmem = 1024 + (size_t)NT * kQBytes + 2 * (size_t)STAGES * kKVBytes + 512;
   static_assert(NT == 1 || kPCol + BN / 2 <= kTileStride, "two query tiles must fit in TMEM");
-  static_assert(kPCol + BN / 2 <= kAttnTmemCols, "query tile must fit in TMEM");
-  static_assert(kSmem <= 232448, "shared memory");
+  static_assert(kPCol + BN / 2 <= kTmemCols, "query tile must fit in TMEM");
+  static_assert(kSmem * kMinBlocks <= 232448, "shared memory");
   static_assert(STAGES <= 4, "barrier slots");
 };
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 256 between rescales
@@ -143,21 +157,14 @@ __device__ __forceinline__ int count_kv_tiles(const int32_t* off, const int32_t*
   return t;
 }
 
-// Register split: the producer/MMA warpgroup gives registers to the two
-// softmax warpgroups.  128*kRegsLow + 256*kRegsHigh must not exceed the
-// registers the CTA is launched with (384 * kLaunchRegs); the launcher checks
-// the kernel's register count before every launch.
-constexpr int kLaunchRegs = 168;
-constexpr int kRegsLow = 56;
-constexpr int kRegsHigh = 224;
-static_assert(128 * kRegsLow + 256 * kRegsHigh <= kAttnThreads * kLaunchRegs, "register split");
-
-template <int DH>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+template <int DH, bool SHORT>
+__global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHORT>::kMinBlocks)
     attention_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ,
                              const __grid_constant__ CUtensorMap tmK,
                              const __grid_constant__ CUtensorMap tmV, const AttnKernelParams p) {
-  using Cfg = AttnCfg<DH>;
+  using Cfg = AttnCfg<DH, SHORT>;
+  constexpr int kRegsLow = Cfg::kRegsLow, kRegsHigh = Cfg::kRegsHigh;
+  constexpr uint32_t kAttnTmemCols = Cfg::kTmemCols;
   constexpr int BN = Cfg::BN, CH = Cfg::CH, NT = Cfg::NT, kKVStages = Cfg::STAGES;
   constexpr uint32_t kQBytes = Cfg::kQBytes, kKVBytes = Cfg::kKVBytes;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -594,9 +601,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // zero-padded to 64, 128 or 256.
 int attn_head_pad(int head_dim) { return head_dim <= 64 ? 64 : (head_dim <= 128 ? 128 : 256); }
 
-template <int DH>
+template <int DH, bool SHORT>
 static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
-  using Cfg = AttnCfg<DH>;
+  using Cfg = AttnCfg<DH, SHORT>;
   CUtensorMap tq, tk, tv;
   {
     uint64_t d[3] = {(uint64_t)DH, (uint64_t)a.q_rows, (uint64_t)a.H};
@@ -623,15 +630,15 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   const int dev = device_index();
   if (!attr_set[dev]) {
     cudaFuncAttributes fa;
-    cudaError_t e0 = cudaFuncGetAttributes(&fa, attention_tcgen05_kernel<DH>);
+    cudaError_t e0 = cudaFuncGetAttributes(&fa, attention_tcgen05_kernel<DH, SHORT>);
     if (e0 != cudaSuccess)
       return set_error(TJ_ERR_CUDA, "attention attributes: %s", cudaGetErrorString(e0));
-    if (fa.numRegs != kLaunchRegs)
+    if (fa.numRegs != Cfg::kLaunchRegs)
       return set_error(TJ_ERR_UNSUPPORTED,
-                       "attention kernel (head dim %d) built with %d registers per thread, the "
+                       "attention kernel (head dim %d%s) built with %d registers per thread, the "
                        "register split assumes %d; refusing to launch",
-                       DH, fa.numRegs, kLaunchRegs);
-    cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel<DH>,
+                       DH, SHORT ? ", short" : "", fa.numRegs, Cfg::kLaunchRegs);
+    cudaError_t e = cudaFuncSetAttribute(attention_tcgen05_kernel<DH, SHORT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
     if (e != cudaSuccess)
       return set_error(TJ_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(e));
@@ -655,7 +662,7 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   dim3 grid((a.max_q_per_sample + kQPerCta - 1) / kQPerCta, a.H, a.B);
   if (grid.y > 65535 || grid.z > 65535)
     return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d or B=%d above 65535", a.H, a.B);
-  cudaError_t e = launch_pdl(attention_tcgen05_kernel<DH>, grid, dim3(kAttnThreads), Cfg::kSmem, stream,
+  cudaError_t e = launch_pdl(attention_tcgen05_kernel<DH, SHORT>, grid, dim3(Cfg::kThreads), Cfg::kSmem, stream,
                              tq, tk, tv, kp);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
@@ -679,11 +686,12 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.q_rows == 0 || a.max_q_per_sample == 0 || a.kv_rows == 0) return TJ_OK;
   switch (attn_head_pad(a.head_dim)) {
     case 64:
-      return launch_attention_t<64>(a, stream);
+      if (a.max_q_per_sample <= kAttnBM) return launch_attention_t<64, true>(a, stream);
+      return launch_attention_t<64, false>(a, stream);
     case 128:
-      return launch_attention_t<128>(a, stream);
+      return launch_attention_t<128, false>(a, stream);
     default:
-      return launch_attention_t<256>(a, stream);
+      return launch_attention_t<256, false>(a, stream);
   }
 }
 
