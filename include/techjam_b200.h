@@ -178,6 +178,19 @@ TJ_API int tj_flash_attn_fwd(const void* q16, const void* k16, const void* v16, 
                       const int32_t* q_cu, const int32_t* kv_off, const int32_t* kv_len,
                       float scale, int causal, const int32_t* q_pos0, void* ctx16, void* stream);
 
+/* tj_flash_attn_fwd with the context row stride given: ctx16 row r, head h
+ * starts at element r*ld_ctx + h*head_dim (ld_ctx >= num_heads*head_dim, a
+ * multiple of 8 when head_dim is; 0 = num_heads*head_dim).  Lets a caller run
+ * attention for a group of heads straight into its columns of a wider
+ * context, e.g. per head group as each group's K/V arrive (the context-
+ * parallel path overlaps the all-gather with attention this way). */
+TJ_API int tj_flash_attn_fwd_strided(const void* q16, const void* k16, const void* v16, int num_heads,
+                              int head_dim, int q_rows, int kv_rows, int64_t kv_stride_h,
+                              int64_t kv_stride_g, int num_segments, int batch, int max_q_per_sample,
+                              const int32_t* q_cu, const int32_t* kv_off, const int32_t* kv_len,
+                              float scale, int causal, const int32_t* q_pos0, void* ctx16,
+                              int64_t ld_ctx, void* stream);
+
 /* ---- whole encoder ----------------------------------------------------- */
 
 typedef struct tj_encoder_desc {

@@ -656,7 +656,7 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   kp.causal = a.causal;
   kp.q_pos0 = a.q_pos0;
   kp.ctx = static_cast<__half*>(a.ctx);
-  kp.ld_ctx = a.H * a.head_dim;
+  kp.ld_ctx = a.ld_ctx ? (int)a.ld_ctx : a.H * a.head_dim;
   kp.dh_out = a.head_dim;
   constexpr int kQPerCta = Cfg::NT * kAttnBM;
   dim3 grid((a.max_q_per_sample + kQPerCta - 1) / kQPerCta, a.H, a.B);
@@ -683,6 +683,12 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
     return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: K/V strides must be multiples of 8 elements");
   if (a.causal && a.G > 1 && a.q_pos0 == nullptr)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: causal with key segments needs q_pos0");
+  if (a.ld_ctx != 0 && (a.ld_ctx < (int64_t)a.H * a.head_dim || a.ld_ctx > INT32_MAX ||
+                        ((a.head_dim & 7) == 0 && (a.ld_ctx & 7) != 0)))
+    return set_error(TJ_ERR_INVALID_ARGUMENT,
+                     "flash_attn_fwd: context row stride %lld (at least H*head_dim = %d, a multiple "
+                     "of 8 when head_dim is)",
+                     (long long)a.ld_ctx, a.H * a.head_dim);
   if (a.q_rows == 0 || a.max_q_per_sample == 0 || a.kv_rows == 0) return TJ_OK;
   switch (attn_head_pad(a.head_dim)) {
     case 64:

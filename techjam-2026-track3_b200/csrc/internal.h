@@ -114,7 +114,8 @@ struct AttnArgs {
   float scale;              // softmax scale (head_dim^-0.5)
   int causal;               // 1: key position > query position masked
   const int32_t* q_pos0;    // causal only: position of the first query of each sample
-  void* ctx;                // fp16 [q_rows][H*dh]
+  void* ctx;                // fp16 [q_rows][ld_ctx]: head h in columns [h*dh, h*dh + dh)
+  int64_t ld_ctx;           // elements between context rows; 0 = H*dh
 };
 
 int launch_attention(const AttnArgs& args, cudaStream_t stream);

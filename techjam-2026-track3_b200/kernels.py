@@ -280,17 +280,23 @@ def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causa
     B = q_cu.numel() - 1
     if out is None:
         out = torch.empty(q.shape[1], H * dh, dtype=torch.float16, device=dev)
-    _require_out(out, "out", (q.shape[1], H * dh), torch.float16, dev)
+    # out may be a column slice of a wider context (a head group's columns):
+    # rows of H*head_dim contiguous halves at any row stride.
+    if not isinstance(out, torch.Tensor) or out.dtype != torch.float16 or out.device != dev:
+        raise TypeError(f"out must be a float16 tensor on {dev}")
+    if tuple(out.shape) != (q.shape[1], H * dh) or out.stride(1) != 1 or out.stride(0) < H * dh:
+        raise ValueError(f"out must be [{q.shape[1]}, {H * dh}] with contiguous rows, got "
+                         f"{tuple(out.shape)} strides {out.stride()}")
     for name, t in (("q_cu", q_cu), ("kv_off", kv_off), ("kv_len", kv_len)):
         _require(t, name, torch.int32, dev)
     if kv_off.numel() != B * G or kv_len.numel() != B * G:
         raise ValueError(f"kv_off/kv_len must hold {B}x{G} entries")
     lib = _lib.load()
-    rc = lib.tj_flash_attn_fwd(
+    rc = lib.tj_flash_attn_fwd_strided(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), H, dh, q.shape[1], kv_rows, k.stride(1),
         k.stride(0), G, B, max_q_per_sample, q_cu.data_ptr(), kv_off.data_ptr(),
         kv_len.data_ptr(), float(scale), 1 if causal else 0, _ptr(q_pos0), out.data_ptr(),
-        _stream(q),
+        out.stride(0), _stream(q),
     )
     _lib.check(rc, "flash_attn_fwd")
     return out

@@ -322,3 +322,25 @@ def test_flash_attention_large_heads(cuda_pkg, dh, H, causal):
     ref = _attn_ref(qkv[0], qkv[1:2], qkv[2:3], cu, kv_off, kv_len, scale, causal=causal, dh=dh)
     assert torch.isfinite(out[:n].float()).all()
     assert float((out[:n].float() - ref[:n]).abs().max()) < 4e-3
+
+
+def test_flash_attention_head_groups_into_strided_context(cuda_pkg):
+    """Attention run per head group straight into its columns of the full
+    context (row stride = all heads), as the context-parallel path does while
+    later groups' K/V are still arriving: equal to one call over all heads."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(5)
+    H, dh = 8, 64
+    lens = torch.tensor([300, 0, 77, 129], dtype=torch.int32)
+    cu = torch.zeros(5, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    rows = int(cu[-1])
+    qkv = torch.randn(3, H, rows, 64, generator=g).half().to(DEV)
+    kv_off, kv_len = cu[:-1].view(-1, 1).contiguous().to(DEV), lens.view(-1, 1).contiguous().to(DEV)
+    cud = cu.to(DEV)
+    full = k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cud, kv_off, kv_len, 300, 0.125)
+    ctx = torch.full((rows, H * dh), float("nan"), dtype=torch.float16, device=DEV)
+    for h0 in range(0, H, 2):
+        k.flash_attn_fwd(qkv[0, h0:h0 + 2], qkv[1:2, h0:h0 + 2].contiguous(), qkv[2:3, h0:h0 + 2].contiguous(),
+                         cud, kv_off, kv_len, 300, 0.125, out=ctx[:, h0 * dh:(h0 + 2) * dh])
+    assert torch.equal(ctx, full)
