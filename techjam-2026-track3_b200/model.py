@@ -319,6 +319,8 @@ class UserOptimizedTransformer(nn.Module):
 
     def _forward_impl(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor]) -> torch.Tensor:
         x, mask = self._check_inputs(x, valid_token_mask)
+        if x.shape[0] == 0 or x.shape[1] == 0:
+            return torch.empty_like(x)  # an empty batch, as the eager model returns
         if (self.use_cuda_graphs and x.numel() * 4 <= self._GRAPH_MAX_INPUT_BYTES
                 and not _lib.sync_check_enabled()
                 and not torch.cuda.is_current_stream_capturing()):

@@ -78,6 +78,7 @@ class BatchShardedEncoder:
         return batch_ranges(batch, self.world)[self.rank]
 
     def forward(self, x_local: torch.Tensor, mask_local: Optional[torch.Tensor], gather: bool = False):
+        # A rank may hold no samples (batch < world); it still joins the gather.
         out = self.model(x_local, mask_local)
         if not gather or self.world == 1:
             return out

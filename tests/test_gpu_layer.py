@@ -156,6 +156,16 @@ def test_two_layers_causal(cuda_pkg):
     _gate(oracle.encoder_forward(sd, cfg, x, mask), out, "2 layers causal")
 
 
+def test_empty_batch(cuda_pkg):
+    """A rank of a batch-sharded job may hold no samples: an empty batch gives an
+    empty output, as the eager reference does."""
+    cfg = oracle.TransformerConfig(2, 128, 256, 4, 1024, 1, False)
+    model = _model(cuda_pkg, cfg, oracle.make_state_dict(cfg, seed=2))
+    x = torch.zeros(0, 128, 256, device=DEV)
+    out = _run(model, x, torch.ones(0, 128, dtype=torch.bool))
+    assert out.shape == (0, 128, 256)
+
+
 def test_rejects_unsupported_inputs(cuda_pkg):
     cfg = oracle.TransformerConfig(1, 128, 256, 4, 1024, 1, False)
     model = _model(cuda_pkg, cfg, oracle.make_state_dict(cfg, seed=1))
