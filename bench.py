@@ -477,6 +477,7 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
     x1 = torch.empty(rows, D, dtype=torch.float32, device=device)
     h16 = torch.empty(rows, F, dtype=torch.float16, device=device)
     y16 = torch.empty(rows, D, dtype=torch.float16, device=device)
+    y16b = torch.empty(rows, D, dtype=torch.float16, device=device)
     out = torch.empty(rows, D, dtype=torch.float32, device=device)
     xf = x.view(rows, D)
     kv_off = cu[:-1].contiguous()
@@ -493,14 +494,15 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
         "gemm_out_f16": (lambda: k.gemm_bias_f16(ctx, att._out_weight_mixed, att.out_proj.bias, row_count=nv_t,
                                                  out=y16), "tensor", 2.0 * nv * D * D),
         "add_ln2_f16": (lambda: k.add_ln_cast_f16(xf, y16, layer.norm2.weight, layer.norm2.bias, row_map=orig,
-                                                  row_count=nv_t, sum_out=x1, out=a16), "hbm", nv * D * (4 + 2 + 4 + 2)),
+                                                  row_count=nv_t, out=a16), "hbm", nv * D * (4 + 2 + 2)),
         "gemm_ffn_in_gelu": (lambda: k.gemm_bias_gelu_f16(a16, layer._ffn_in_weight_mixed, layer.ffn_in.bias,
                                                           row_count=nv_t, out=h16), "tensor", 2.0 * nv * F * D),
         "gemm_ffn_out_f16": (lambda: k.gemm_bias_f16(h16, layer._ffn_out_weight_mixed, layer.ffn_out.bias,
-                                                     row_count=nv_t, out=y16), "tensor", 2.0 * nv * D * F),
-        "add_ln_final_mask": (lambda: k.add_ln_final_mask(x1, y16, model.final_norm.weight, model.final_norm.bias,
-                                                          inv_map=inv, rows=rows, out=out), "hbm",
-                              nv * D * (4 + 2 + 4) + (rows - nv) * D * 4),
+                                                     row_count=nv_t, out=y16b), "tensor", 2.0 * nv * D * F),
+        "add2_ln_final_mask": (lambda: k.add2_ln_final_mask(xf, y16, y16b, model.final_norm.weight,
+                                                            model.final_norm.bias, inv_map=inv,
+                                                            x_at_original=True, rows=rows, out=out), "hbm",
+                               nv * D * (4 + 2 + 2 + 4) + (rows - nv) * D * 4),
     }
     reps = max(3, min(50, args.steps))
     res = {}

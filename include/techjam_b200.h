@@ -89,6 +89,8 @@ TJ_API int64_t tj_token_plan_ints(int batch, int seq_len);
  *   plan[B+2 .. 2B+1]            per-sample valid counts
  *   plan[2B+2 .. 2B+2+BS)        compact row -> original row b*S+s
  *   plan[2B+2+BS .. 2B+2+2BS)    original row -> compact row, or -1 if padded
+ *   plan[2B+2+2BS .. 3B+2+2BS)   samples by decreasing valid count (stable;
+ *                                identity when batch > 256)
  * Replaces the mask plumbing of v16_1_clean.py:607-611 (key mask [B,1,1,S] and
  * query mask [B,S,1]); padded tokens then never enter a GEMM or attention. */
 TJ_API int tj_token_plan(const uint8_t* mask, int batch, int seq_len, int32_t* plan, void* stream);
@@ -126,6 +128,16 @@ TJ_API int tj_add_ln_cast_f16(const float* x, const int32_t* row_map, const void
 TJ_API int tj_add_ln_final_mask(const float* x, const void* add16, const int32_t* inv_map, int rows,
                          int d_model, const float* gamma, const float* beta, float eps, float* out,
                          void* stream);
+
+/* out[m] = LayerNorm((x[r] + float(attn16[c])) + float(ffn16[c])) with
+ * c = inv_map[m] >= 0 and r = m if x_at_original else c; exact zeros where
+ * inv_map[m] < 0.  The last layer's two residual adds (:620-621) fused with
+ * final_norm + masked_fill (:625-627), so x + attention is never stored; with
+ * one layer x is the encoder input itself, read at the original row. */
+TJ_API int tj_add2_ln_final_mask(const float* x, int x_at_original, const void* attn16,
+                          const void* ffn16, const int32_t* inv_map, int rows, int d_model,
+                          const float* gamma, const float* beta, float eps, float* out,
+                          void* stream);
 
 /* qkv16 (head-major [3][H][rows_max][P], see above) = fp16(a16 @ w_qkv^T + b_qkv) for the
  * first min(rows_max, *row_count) rows; w_qkv is the packed [3D, D] q/k/v

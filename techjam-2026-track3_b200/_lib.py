@@ -79,6 +79,10 @@ SIGNATURES = {
         c_int,
         [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp, c_vp],
     ),
+    "tj_add2_ln_final_mask": (
+        c_int,
+        [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp],
+    ),
     "tj_add_ln_final_mask": (
         c_int,
         [c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp],

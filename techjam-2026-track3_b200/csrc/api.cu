@@ -68,7 +68,7 @@ static int check_device() {
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct EncoderWorkspace {
-  size_t plan, a16, qkv16, x1, x2, h16, y16, total;
+  size_t plan, a16, qkv16, x1, x2, h16, y16, y16b, total;
 };
 
 static bool workspace_layout(const tj_encoder_desc* d, EncoderWorkspace* w) {
@@ -91,6 +91,8 @@ static bool workspace_layout(const tj_encoder_desc* d, EncoderWorkspace* w) {
   w->h16 = off;
   off = align_up(off + rows * F * 2, 256);
   w->y16 = off;  // fp16 output of the out-projection / FFN-out before its residual add
+  off = align_up(off + rows * D * 2, 256);
+  w->y16b = off;  // the last layer's FFN-out (its out-projection output stays in y16)
   off = align_up(off + rows * D * 2, 256);
   w->total = off;
   return true;
@@ -173,6 +175,21 @@ int tj_add_ln_cast_f16(const float* x, const int32_t* row_map, const void* add16
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return finish(launch_ln_cast_f16(x, row_map, row_count, rows, d_model, gamma, beta, eps, y16, s,
                                    add16, sum_out),
+                s);
+}
+
+int tj_add2_ln_final_mask(const float* x, int x_at_original, const void* attn16,
+                          const void* ffn16, const int32_t* inv_map, int rows, int d_model,
+                          const float* gamma, const float* beta, float eps, float* out,
+                          void* stream) {
+  int rc = check_device();
+  if (rc) return rc;
+  if (!attn16 || !ffn16) return set_error(TJ_ERR_INVALID_ARGUMENT, "add2_ln_final_mask: null addend");
+  if (x_at_original && !inv_map)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "add2_ln_final_mask: x_at_original needs inv_map");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return finish(launch_ln_final(x, inv_map, rows, d_model, gamma, beta, eps, out, s, attn16, ffn16,
+                                x_at_original != 0),
                 s);
 }
 
@@ -353,6 +370,7 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
   float* x2 = reinterpret_cast<float*>(ws + w.x2);
   __half* h16 = reinterpret_cast<__half*>(ws + w.h16);
   __half* y16 = reinterpret_cast<__half*>(ws + w.y16);
+  __half* y16b = reinterpret_cast<__half*>(ws + w.y16b);
   const int32_t* nv = plan.nv();
 
   rc = launch_token_plan(mask, B, S, plan.base, s);
@@ -360,9 +378,13 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
   // Residual stream (fp32, compact rows): layer 0 reads the input through the
   // plan's row map; afterwards x1 holds x after attention and x2 the input of
   // the next layer.  The out-projection and FFN-out leave their fp16 result in
-  // y16 and the next LayerNorm kernel adds it to the stream.
+  // y16 and the next LayerNorm kernel adds it to the stream.  In the last
+  // layer the sum x + attention is not stored: the final LayerNorm adds both
+  // fp16 branch outputs (y16, y16b) to the layer input itself, which saves
+  // the fp32 write and read of x1.
   for (int l = 0; l < d->num_layers; ++l) {
     const tj_layer_weights& L = layers[l];
+    const bool last = l + 1 == d->num_layers;
     const float* xin = (l == 0) ? x : x2;
     const int32_t* in_map = (l == 0) ? plan.orig() : nullptr;
     if (l == 0)
@@ -404,6 +426,7 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     a.scale = 1.0f / sqrtf((float)dh);
     a.causal = d->causal;
     a.q_pos0 = nullptr;
+    a.order = plan.order();
     a.ctx = a16;  // LN1 output is dead once the QKV GEMM has run
     rc = launch_attention(a, s);
     if (rc) return rc;
@@ -421,7 +444,7 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     if (rc) return rc;
     // x1 = x + attention output; a16 = LN2(x1)
     rc = launch_ln_cast_f16(xin, in_map, nv, rows, D, L.ln2_gamma, L.ln2_beta, d->ln_eps, a16, s, y16,
-                            x1);
+                            last ? nullptr : x1);
     if (rc) return rc;
     GemmArgs f1{};
     f1.a16 = a16;
@@ -443,13 +466,17 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     f2.rows_max = rows;
     f2.N = D;
     f2.K = F;
-    f2.out = y16;
+    f2.out = last ? y16b : y16;
     f2.ld_out = D;
     rc = launch_gemm(kEpiBiasF16, f2, s);
     if (rc) return rc;
   }
-  // out = final LN(x1 + FFN-out), scattered to the original rows
-  rc = launch_ln_final(x1, plan.inv(), rows, D, final_gamma, final_beta, d->ln_eps, out, s, y16);
+  // out = final LN((x + attention output) + FFN-out) of the last layer,
+  // scattered to the original rows; x is the input itself (one layer, read
+  // at the output row) or the last layer's compact input x2.
+  const bool one_layer = d->num_layers == 1;
+  rc = launch_ln_final(one_layer ? x : x2, plan.inv(), rows, D, final_gamma, final_beta, d->ln_eps, out,
+                       s, y16, y16b, one_layer);
   return finish(rc, s);
 }
 

@@ -99,6 +99,7 @@ struct AttnKernelParams {
   __half* ctx;
   int ld_ctx;
   int dh_out;  // real head dim (<= DH): columns of ctx written per head
+  const int32_t* order;  // optional: sample handled by grid row z (longest first)
 };
 
 // Walks the key tiles of one sample in order: segment g, tile i inside it.
@@ -167,8 +168,9 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
   constexpr uint32_t kAttnTmemCols = Cfg::kTmemCols;
   constexpr int BN = Cfg::BN, CH = Cfg::CH, NT = Cfg::NT, kKVStages = Cfg::STAGES;
   constexpr uint32_t kQBytes = Cfg::kQBytes, kKVBytes = Cfg::kKVBytes;
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int h = blockIdx.y;
   pdl_wait();  // q/k/v and the token plan come from earlier kernels
+  const int b = p.order ? p.order[blockIdx.z] : (int)blockIdx.z;
   const int q_begin = p.q_cu[b];
   const int nq = p.q_cu[b + 1] - q_begin;
   const int q_tile0 = blockIdx.x * NT;
@@ -658,6 +660,7 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   kp.ctx = static_cast<__half*>(a.ctx);
   kp.ld_ctx = a.ld_ctx ? (int)a.ld_ctx : a.H * a.head_dim;
   kp.dh_out = a.head_dim;
+  kp.order = a.order;
   constexpr int kQPerCta = Cfg::NT * kAttnBM;
   dim3 grid((a.max_q_per_sample + kQPerCta - 1) / kQPerCta, a.H, a.B);
   if (grid.y > 65535 || grid.z > 65535)

@@ -50,6 +50,8 @@ int64_t plan_ints(int B, int S);
 //   [B+2, B+2+B)        n   (valid tokens per sample)
 //   [2B+2, 2B+2+BS)     orig (compact row -> original row b*S+s)
 //   [2B+2+BS, ...+BS)   inv  (original row -> compact row, or -1)
+//   [2B+2+2BS, ...+B)   order (samples by decreasing valid count; identity
+//                        for batches above 256)
 struct PlanView {
   int32_t* base;
   int B, S;
@@ -58,6 +60,7 @@ struct PlanView {
   int32_t* n() const { return base + 2 + B; }
   int32_t* orig() const { return base + 2 + 2 * B; }
   int32_t* inv() const { return base + 2 + 2 * B + (int64_t)B * S; }
+  int32_t* order() const { return base + 2 + 2 * B + 2 * (int64_t)B * S; }
 };
 
 int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStream_t stream);
@@ -68,9 +71,12 @@ int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* ro
                        int D, const float* gamma, const float* beta, float eps, void* y16,
                        cudaStream_t stream, const void* add16 = nullptr, float* sum_out = nullptr);
 
+// add16b (optional) is a second fp16 addend; with x_at_original, x is read
+// at the output row m instead of the compact row inv_map[m].
 int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
                     const float* beta, float eps, float* out, cudaStream_t stream,
-                    const void* add16 = nullptr);
+                    const void* add16 = nullptr, const void* add16b = nullptr,
+                    bool x_at_original = false);
 
 enum GemmEpilogue : int {
   kEpiQkvHeadMajor = 0,   // fp16 out, head-major [3][H][rows_max][attn_head_pad(dh)]
@@ -114,6 +120,7 @@ struct AttnArgs {
   float scale;              // softmax scale (head_dim^-0.5)
   int causal;               // 1: key position > query position masked
   const int32_t* q_pos0;    // causal only: position of the first query of each sample
+  const int32_t* order;     // optional [B]: sample of each grid row (longest first)
   void* ctx;                // fp16 [q_rows][ld_ctx]: head h in columns [h*dh, h*dh + dh)
   int64_t ld_ctx;           // elements between context rows; 0 = H*dh
 };

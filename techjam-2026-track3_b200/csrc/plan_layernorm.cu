@@ -29,6 +29,7 @@ namespace tj {
 // re-reads the segment and writes orig/inv/cu coalesced.
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanOrderMaxB = 256;  // batches up to this size get a longest-first order
 constexpr int kPlanBatch = 16;  // 32-byte groups loaded per batch
 
 // Valid flags of groups g0 .. g0+15 of the warp's segment, bit k for group k.
@@ -117,12 +118,33 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
   }
   __syncthreads();
   __threadfence_block();
-  for (int b = threadIdx.x; b < B; b += kPlanThreads)
-    cnt[b] = ((volatile int32_t*)cu)[b + 1] - ((volatile int32_t*)cu)[b];
+  int32_t* order = inv + total;
+  __shared__ int cnt_s[kPlanOrderMaxB];
+  for (int b = threadIdx.x; b < B; b += kPlanThreads) {
+    const int c = ((volatile int32_t*)cu)[b + 1] - ((volatile int32_t*)cu)[b];
+    cnt[b] = c;
+    if (B <= kPlanOrderMaxB) cnt_s[b] = c;
+  }
+  // Samples by decreasing valid-token count (stable): attention launches its
+  // CTAs for the longest samples first, so the last wave holds short ones.
+  if (B <= kPlanOrderMaxB) {
+    __syncthreads();
+    for (int b = threadIdx.x; b < B; b += kPlanThreads) {
+      const int c = cnt_s[b];
+      int rank = 0;
+      for (int o = 0; o < B; ++o) {
+        const int co = cnt_s[o];
+        rank += (co > c || (co == c && o < b)) ? 1 : 0;
+      }
+      order[rank] = b;
+    }
+  } else {
+    for (int b = threadIdx.x; b < B; b += kPlanThreads) order[b] = b;
+  }
   pdl_trigger();
 }
 
-int64_t plan_ints(int B, int S) { return 2 + 2 * (int64_t)B + 2 * (int64_t)B * S; }
+int64_t plan_ints(int B, int S) { return 2 + 3 * (int64_t)B + 2 * (int64_t)B * S; }
 
 int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStream_t stream) {
   if (B <= 0 || S <= 0) return set_error(TJ_ERR_INVALID_ARGUMENT, "token_plan: B=%d S=%d", B, S);
@@ -231,9 +253,13 @@ __global__ void __launch_bounds__(256) ln_cast_f16_kernel(
   }
 }
 
+// out[m] = LayerNorm(x + add16[c] (+ add16b[c])) for c = inv_map[m] >= 0 (x
+// read at row c, or at row m with x_at_original), exact zeros otherwise.
 template <int VPL>
 __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__ x,
                                                        const __half* __restrict__ add16,
+                                                       const __half* __restrict__ add16b,
+                                                       int x_at_original,
                                                        const int32_t* __restrict__ inv_map,
                                                        int rows, int D,
                                                        const float* __restrict__ gamma,
@@ -254,7 +280,7 @@ __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__
     }
     return;
   }
-  const float4* xr = reinterpret_cast<const float4*>(x + src * D);
+  const float4* xr = reinterpret_cast<const float4*>(x + (x_at_original ? (int64_t)row : src) * D);
   float4 v[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
@@ -262,6 +288,7 @@ __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__
     v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (add16) add_f16_row<VPL>(v, add16 + src * D, D, lane);
+  if (add16b) add_f16_row<VPL>(v, add16b + src * D, D, lane);
   float mean, rstd;
   ln_row_stats<VPL>(v, D, lane, mean, rstd, eps);
 #pragma unroll
@@ -323,22 +350,25 @@ int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* ro
 
 int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
                     const float* beta, float eps, float* out, cudaStream_t stream,
-                    const void* add16) {
+                    const void* add16, const void* add16b, bool x_at_original) {
   if (rows < 0 || D <= 0 || D % 4 != 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
   const int vpl = ln_vpl(D);
   if (vpl < 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_final_mask: D=%d above 4096", D);
   if (!x || !gamma || !beta || !out || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
-      !aligned16(out) || (reinterpret_cast<uintptr_t>(add16) & 7u))
+      !aligned16(out) || (reinterpret_cast<uintptr_t>(add16) & 7u) ||
+      (reinterpret_cast<uintptr_t>(add16b) & 7u) || (add16b && !add16))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: null or misaligned pointer");
   if (rows == 0) return TJ_OK;
   const int warps = 8;
   dim3 grid((rows + warps - 1) / warps);
   const __half* add = static_cast<const __half*>(add16);
+  const __half* addb = static_cast<const __half*>(add16b);
+  const int xo = x_at_original ? 1 : 0;
   cudaError_t e = cudaSuccess;
   switch (vpl) {
 #define TJ_LN_CASE(V) \
-  case V: e = launch_pdl(ln_final_kernel<V>, grid, dim3(warps * 32), 0, stream, x, add, inv_map, rows, D, gamma, beta, eps, out); break;
+  case V: e = launch_pdl(ln_final_kernel<V>, grid, dim3(warps * 32), 0, stream, x, add, addb, xo, inv_map, rows, D, gamma, beta, eps, out); break;
     TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
 #undef TJ_LN_CASE
   }

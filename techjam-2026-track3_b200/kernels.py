@@ -70,7 +70,8 @@ def token_plan(mask: Optional[torch.Tensor], batch: int, seq_len: int, device) -
 
 
 def plan_views(plan: torch.Tensor, batch: int, seq_len: int):
-    """(nv[1], cu[B+1], counts[B], orig[BS], inv[BS]) views of a token plan."""
+    """(nv[1], cu[B+1], counts[B], orig[BS], inv[BS]) views of a token plan (it
+    ends with order[B], the samples by decreasing count: plan_order)."""
     B, BS = batch, batch * seq_len
     nv = plan[0:1]
     cu = plan[1 : B + 2]
@@ -78,6 +79,13 @@ def plan_views(plan: torch.Tensor, batch: int, seq_len: int):
     orig = plan[2 * B + 2 : 2 * B + 2 + BS]
     inv = plan[2 * B + 2 + BS : 2 * B + 2 + 2 * BS]
     return nv, cu, cnt, orig, inv
+
+
+def plan_order(plan: torch.Tensor, batch: int, seq_len: int) -> torch.Tensor:
+    """order[B] of a token plan: samples by decreasing valid count (stable;
+    the identity for batches above 256)."""
+    off = 2 * batch + 2 + 2 * batch * seq_len
+    return plan[off : off + batch]
 
 
 def ln_cast_f16(x, gamma, beta, eps=1e-5, row_map=None, row_count=None, out=None):
@@ -164,6 +172,33 @@ def add_ln_final_mask(x, add16, gamma, beta, eps=1e-5, inv_map=None, rows=None, 
         float(eps), out.data_ptr(), _stream(x),
     )
     _lib.check(rc, "add_ln_final_mask")
+    return out
+
+
+def add2_ln_final_mask(x, attn16, ffn16, gamma, beta, eps=1e-5, inv_map=None, x_at_original=False,
+                       rows=None, out=None):
+    """out[m] = LayerNorm((x[r] + attn16[c]) + ffn16[c]), c = inv_map[m], r = m if
+    x_at_original else c (zeros where c < 0)."""
+    dev = x.device
+    _require(x, "x", torch.float32, dev)
+    _require(attn16, "attn16", torch.float16, dev)
+    _require(ffn16, "ffn16", torch.float16, dev)
+    D = x.shape[-1]
+    if attn16.shape != ffn16.shape or attn16.dim() != 2 or attn16.shape[1] != D:
+        raise ValueError("attn16 and ffn16 must both be [compact_rows, D]")
+    if rows is None:
+        rows = x.numel() // D if inv_map is None else inv_map.numel()
+    if x_at_original and (inv_map is None or x.numel() // D < rows):
+        raise ValueError("x_at_original needs inv_map and x holding every output row")
+    if out is None:
+        out = torch.empty(rows, D, dtype=torch.float32, device=dev)
+    _require_out(out, "out", (rows, D), torch.float32, dev)
+    lib = _lib.load()
+    rc = lib.tj_add2_ln_final_mask(
+        x.data_ptr(), 1 if x_at_original else 0, attn16.data_ptr(), ffn16.data_ptr(), _ptr(inv_map), rows,
+        D, gamma.data_ptr(), beta.data_ptr(), float(eps), out.data_ptr(), _stream(x),
+    )
+    _lib.check(rc, "add2_ln_final_mask")
     return out
 
 

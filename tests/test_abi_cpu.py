@@ -40,7 +40,7 @@ def test_library_exports_every_symbol(pkg):
 
 def test_argument_errors_are_reported_without_gpu(pkg):
     lib = pkg._lib.load()
-    assert lib.tj_token_plan_ints(2, 8) == 2 + 2 * 2 + 2 * 16
+    assert lib.tj_token_plan_ints(2, 8) == 2 + 3 * 2 + 2 * 16  # nv, cu, counts, orig, inv, order
     assert lib.tj_token_plan_ints(0, 8) == 0
     desc = pkg._lib.EncoderDesc(8, 2048, 1024, 16, 4096, 1, 0, 1e-5)
     need = lib.tj_encoder_workspace_bytes(ctypes.byref(desc))

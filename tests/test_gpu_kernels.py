@@ -52,6 +52,12 @@ def test_token_plan(cuda_pkg, B, S):
     assert torch.equal(cnt, r_cnt)
     assert torch.equal(orig[: int(nv)], r_orig)
     assert torch.equal(inv, r_inv)
+    order = k.plan_order(plan, B, S).cpu()
+    if B <= 256:  # longest first, ties by sample index
+        ref_order = sorted(range(B), key=lambda b: (-int(r_cnt[b]), b))
+        assert order.tolist() == ref_order
+    else:
+        assert torch.equal(order, torch.arange(B, dtype=torch.int32))
     # No mask: identity plan.
     plan = k.token_plan(None, B, S, DEV)
     nv, cu, cnt, orig, inv = [t.cpu() for t in k.plan_views(plan, B, S)]
@@ -117,6 +123,35 @@ def test_add_ln_cast_and_final(cuda_pkg, rows, D):
     inv[slots] = torch.arange(rows, dtype=torch.int32)
     out = k.add_ln_final_mask(xc.to(DEV), ad, gd, bd, inv_map=inv.to(DEV)).cpu().double()
     torch.testing.assert_close(out[slots], ref2, rtol=0, atol=2e-5)
+    assert torch.count_nonzero(out[inv < 0]) == 0
+
+
+@pytest.mark.parametrize("x_at_original", [True, False])
+def test_add2_ln_final(cuda_pkg, x_at_original):
+    """The last layer's two residual adds fused with the final LayerNorm and the
+    scatter: LN((x + attn) + ffn), x read at the output row or the compact row."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(3 + int(x_at_original))
+    rows, D = 700, 1024
+    inv = torch.full((rows,), -1, dtype=torch.int32)
+    valid = torch.randperm(rows, generator=g)[:500].sort().values
+    inv[valid] = torch.arange(500, dtype=torch.int32)
+    nvr = 500
+    attn = (torch.randn(nvr, D, generator=g) * 2).half()
+    ffn = (torch.randn(nvr, D, generator=g) * 2).half()
+    gamma = 1 + 0.1 * torch.randn(D, generator=g)
+    beta = 0.1 * torch.randn(D, generator=g)
+    if x_at_original:
+        x = torch.randn(rows, D, generator=g) * 3
+        xs = x[valid]
+    else:
+        x = torch.randn(nvr, D, generator=g) * 3
+        xs = x
+    s_ref = (xs + attn.float()) + ffn.float()
+    ref = torch.nn.functional.layer_norm(s_ref.double(), (D,), gamma.double(), beta.double(), 1e-5)
+    out = k.add2_ln_final_mask(x.to(DEV), attn.to(DEV), ffn.to(DEV), gamma.to(DEV), beta.to(DEV),
+                               inv_map=inv.to(DEV), x_at_original=x_at_original, rows=rows).cpu().double()
+    torch.testing.assert_close(out[valid], ref, rtol=0, atol=2e-5)
     assert torch.count_nonzero(out[inv < 0]) == 0
 
 
