@@ -391,7 +391,7 @@ def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
     Steps are pipelined the way a serving loop runs them: the upload of step
     i+1 and the download of step i-1 (two copy streams) overlap the forward of
     step i (compute stream), with events ordering each step's three stages."""
-    steps = max(3, min(args.steps, 30))
+    steps = max(3, min(args.steps, 60))  # the pipeline fills and drains once per run
     nbuf = 3
     x_host = [x_cpu.clone().pin_memory() for _ in range(nbuf)]
     m_host = mask_cpu.pin_memory()
