@@ -357,6 +357,11 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
   const int dh = D / H;
   if (dh > 256)
     return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: head_dim %d (1..256 supported)", dh);
+  // fp16 GEMM operand rows must be whole 16-byte units for their TMA loads.
+  if (D % 8 != 0 || F % 8 != 0)
+    return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: d_model %d and ffn_dim %d must be multiples of 8", D, F);
+  if (D > 32768)
+    return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: d_model %d above 32768", D);
   const int kPad = attn_head_pad(dh);  // head-major row length of the QKV buffer
   if ((int64_t)B * S > INT32_MAX / 4)
     return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: B*S too large");

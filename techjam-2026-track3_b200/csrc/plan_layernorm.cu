@@ -158,40 +158,60 @@ int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStre
 }
 
 // ---------------------------------------------------------------------------
-// LayerNorm.  One warp per row; lane l holds float4 groups l, l+32, ... of the
-// row (VPL groups per lane, so D <= 128 * VPL).
+// LayerNorm.  RT threads per row: one warp (RT = 32, D <= 4096) or a whole
+// CTA of 256 threads (RT = 256, wider rows up to 32768).  Thread k of a row
+// holds float4 groups k, k+RT, ... (VPL groups, so D <= 4 * RT * VPL), and
+// the row stays in registers between the mean and the variance pass.
 // ---------------------------------------------------------------------------
-template <int VPL>
-__device__ __forceinline__ void ln_row_stats(const float4 (&v)[VPL], int D, int lane, float& mean,
-                                             float& rstd, float eps) {
+constexpr int kLnThreads = 256;
+constexpr int kLnWideMaxD = 4 * kLnThreads * 32;
+
+// Sum over the RT threads of a row (all of them get it).  RT = 256 goes
+// through `red` (kLnThreads / 32 floats of shared memory), and every thread
+// of the CTA must call it.
+template <int RT>
+__device__ __forceinline__ float ln_row_sum(float s, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if constexpr (RT > 32) {
+    constexpr int kWarps = RT / 32;
+    __syncthreads();  // an earlier sum may still be reading red
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red[w];
+  }
+  return s;
+}
+
+template <int VPL, int RT>
+__device__ __forceinline__ void ln_row_stats(const float4 (&v)[VPL], int D, int k, float& mean,
+                                             float& rstd, float eps, float* red) {
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    if ((i * 32 + lane) * 4 < D) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    if ((i * RT + k) * 4 < D) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  mean = s / (float)D;
+  mean = ln_row_sum<RT>(s, red) / (float)D;
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    if ((i * 32 + lane) * 4 < D) {
+    if ((i * RT + k) * 4 < D) {
       const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
       q += (a * a + b * b) + (c * c + d * d);
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  rstd = 1.0f / sqrtf(q / (float)D + eps);
+  rstd = 1.0f / sqrtf(ln_row_sum<RT>(q, red) / (float)D + eps);
 }
 
 // v[i] += the four fp16 values of group g of an addend row (fp32 sum).
-template <int VPL>
-__device__ __forceinline__ void add_f16_row(float4 (&v)[VPL], const __half* add_row, int D, int lane) {
+template <int VPL, int RT>
+__device__ __forceinline__ void add_f16_row(float4 (&v)[VPL], const __half* add_row, int D, int k) {
   const uint2* ar = reinterpret_cast<const uint2*>(add_row);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    const int g = i * 32 + lane;
+    const int g = i * RT + k;
     if (g * 4 < D) {
       const uint2 u = __ldg(ar + g);
       const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
@@ -207,41 +227,42 @@ __device__ __forceinline__ void add_f16_row(float4 (&v)[VPL], const __half* add_
 // y[r] = fp16(LayerNorm(x[row_map[r]] (+ add16[r]))), and with sum_out the
 // fp32 row x[row_map[r]] + add16[r] is stored to sum_out[r] (the residual
 // stream after a branch whose output the GEMM left in fp16).
-template <int VPL>
-__global__ void __launch_bounds__(256) ln_cast_f16_kernel(
+template <int VPL, int RT>
+__global__ void __launch_bounds__(kLnThreads) ln_cast_f16_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ row_map,
     const __half* __restrict__ add16, const int32_t* __restrict__ row_count, int rows, int D,
     const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
     float* __restrict__ sum_out, __half* __restrict__ y) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  __shared__ float red[kLnThreads / 32];
+  const int k = (int)threadIdx.x % RT;
+  const int row = blockIdx.x * (kLnThreads / RT) + (int)threadIdx.x / RT;
   pdl_wait();
   pdl_trigger();
   const int limit = row_count ? min(rows, *row_count) : rows;
-  if (row >= limit) return;
+  if (row >= limit) return;  // uniform for the RT threads of a row
   const int64_t src = row_map ? (int64_t)row_map[row] : (int64_t)row;
   const float4* xr = reinterpret_cast<const float4*>(x + src * D);
   float4 v[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    const int g = i * 32 + lane;
+    const int g = i * RT + k;
     v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  if (add16) add_f16_row<VPL>(v, add16 + (int64_t)row * D, D, lane);
+  if (add16) add_f16_row<VPL, RT>(v, add16 + (int64_t)row * D, D, k);
   if (sum_out) {
     float4* sr = reinterpret_cast<float4*>(sum_out + (int64_t)row * D);
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
-      const int g = i * 32 + lane;
+      const int g = i * RT + k;
       if (g * 4 < D) sr[g] = v[i];
     }
   }
   float mean, rstd;
-  ln_row_stats<VPL>(v, D, lane, mean, rstd, eps);
+  ln_row_stats<VPL, RT>(v, D, k, mean, rstd, eps, red);
   uint2* yr = reinterpret_cast<uint2*>(y + (int64_t)row * D);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    const int g = i * 32 + lane;
+    const int g = i * RT + k;
     if (g * 4 < D) {
       const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma) + g);
       const float4 be = __ldg(reinterpret_cast<const float4*>(beta) + g);
@@ -255,27 +276,28 @@ __global__ void __launch_bounds__(256) ln_cast_f16_kernel(
 
 // out[m] = LayerNorm(x + add16[c] (+ add16b[c])) for c = inv_map[m] >= 0 (x
 // read at row c, or at row m with x_at_original), exact zeros otherwise.
-template <int VPL>
-__global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__ x,
-                                                       const __half* __restrict__ add16,
-                                                       const __half* __restrict__ add16b,
-                                                       int x_at_original,
-                                                       const int32_t* __restrict__ inv_map,
-                                                       int rows, int D,
-                                                       const float* __restrict__ gamma,
-                                                       const float* __restrict__ beta, float eps,
-                                                       float* __restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+template <int VPL, int RT>
+__global__ void __launch_bounds__(kLnThreads) ln_final_kernel(const float* __restrict__ x,
+                                                              const __half* __restrict__ add16,
+                                                              const __half* __restrict__ add16b,
+                                                              int x_at_original,
+                                                              const int32_t* __restrict__ inv_map,
+                                                              int rows, int D,
+                                                              const float* __restrict__ gamma,
+                                                              const float* __restrict__ beta, float eps,
+                                                              float* __restrict__ out) {
+  __shared__ float red[kLnThreads / 32];
+  const int k = (int)threadIdx.x % RT;
+  const int row = blockIdx.x * (kLnThreads / RT) + (int)threadIdx.x / RT;
   pdl_wait();
   pdl_trigger();
-  if (row >= rows) return;
+  if (row >= rows) return;  // uniform for the RT threads of a row
   const int64_t src = inv_map ? (int64_t)inv_map[row] : (int64_t)row;
   float4* orow = reinterpret_cast<float4*>(out + (int64_t)row * D);
   if (src < 0) {  // padded token: exact zero, as masked_fill(~mask, 0) gives
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
-      const int g = i * 32 + lane;
+      const int g = i * RT + k;
       if (g * 4 < D) orow[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     return;
@@ -284,16 +306,16 @@ __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__
   float4 v[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    const int g = i * 32 + lane;
+    const int g = i * RT + k;
     v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  if (add16) add_f16_row<VPL>(v, add16 + src * D, D, lane);
-  if (add16b) add_f16_row<VPL>(v, add16b + src * D, D, lane);
+  if (add16) add_f16_row<VPL, RT>(v, add16 + src * D, D, k);
+  if (add16b) add_f16_row<VPL, RT>(v, add16b + src * D, D, k);
   float mean, rstd;
-  ln_row_stats<VPL>(v, D, lane, mean, rstd, eps);
+  ln_row_stats<VPL, RT>(v, D, k, mean, rstd, eps, red);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    const int g = i * 32 + lane;
+    const int g = i * RT + k;
     if (g * 4 < D) {
       const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma) + g);
       const float4 be = __ldg(reinterpret_cast<const float4*>(beta) + g);
@@ -307,15 +329,16 @@ __global__ void __launch_bounds__(256) ln_final_kernel(const float* __restrict__
   }
 }
 
-static int ln_vpl(int D) {
-  const int groups = (D / 4 + 31) / 32;
-  if (groups <= 1) return 1;
-  if (groups <= 2) return 2;
-  if (groups <= 4) return 4;
-  if (groups <= 8) return 8;
-  if (groups <= 16) return 16;
-  if (groups <= 32) return 32;
-  return -1;
+// Groups of 4 columns per thread for a row of D columns: a warp per row up to
+// D = 4096 (VPL 1..32), then a CTA per row (VPL 8, 16, 32 of 256 threads).
+// Returns 0 when D is above kLnWideMaxD.
+static int ln_vpl(int D, bool* wide) {
+  const int groups = D / 4;
+  *wide = groups > 32 * 32;
+  const int per = *wide ? (groups + kLnThreads - 1) / kLnThreads : (groups + 31) / 32;
+  for (int v = 1; v <= 32; v *= 2)
+    if (per <= v) return *wide && v < 8 ? 8 : v;
+  return 0;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -325,24 +348,38 @@ int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* ro
                        cudaStream_t stream, const void* add16, float* sum_out) {
   if (rows < 0 || D <= 0 || D % 4 != 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
-  const int vpl = ln_vpl(D);
-  if (vpl < 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_cast_f16: D=%d above 4096", D);
+  bool wide = false;
+  const int vpl = ln_vpl(D, &wide);
+  if (vpl == 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_cast_f16: D=%d above %d", D, kLnWideMaxD);
   if (!x || !gamma || !beta || !y16 || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
       (reinterpret_cast<uintptr_t>(y16) & 7u) || (reinterpret_cast<uintptr_t>(add16) & 7u) ||
       !aligned16(sum_out))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: null or misaligned pointer");
   if (rows == 0) return TJ_OK;
-  const int warps = 8;
-  dim3 grid((rows + warps - 1) / warps);
+  const int per_cta = wide ? 1 : kLnThreads / 32;
+  dim3 grid((rows + per_cta - 1) / per_cta);
   __half* y = static_cast<__half*>(y16);
   const __half* add = static_cast<const __half*>(add16);
   cudaError_t e = cudaSuccess;
-  switch (vpl) {
-#define TJ_LN_CASE(V) \
-  case V: e = launch_pdl(ln_cast_f16_kernel<V>, grid, dim3(warps * 32), 0, stream, x, row_map, add, row_count, rows, D, gamma, beta, eps, sum_out, y); break;
-    TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
-#undef TJ_LN_CASE
+#define TJ_LN_CASE(V, R) \
+  e = launch_pdl(ln_cast_f16_kernel<V, R>, grid, dim3(kLnThreads), 0, stream, x, row_map, add, row_count, rows, D, gamma, beta, eps, sum_out, y)
+  if (!wide) {
+    switch (vpl) {
+      case 1: TJ_LN_CASE(1, 32); break;
+      case 2: TJ_LN_CASE(2, 32); break;
+      case 4: TJ_LN_CASE(4, 32); break;
+      case 8: TJ_LN_CASE(8, 32); break;
+      case 16: TJ_LN_CASE(16, 32); break;
+      default: TJ_LN_CASE(32, 32); break;
+    }
+  } else {
+    switch (vpl) {
+      case 8: TJ_LN_CASE(8, kLnThreads); break;
+      case 16: TJ_LN_CASE(16, kLnThreads); break;
+      default: TJ_LN_CASE(32, kLnThreads); break;
+    }
   }
+#undef TJ_LN_CASE
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_cast_f16 launch: %s", cudaGetErrorString(e));
   return TJ_OK;
@@ -353,25 +390,39 @@ int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, con
                     const void* add16, const void* add16b, bool x_at_original) {
   if (rows < 0 || D <= 0 || D % 4 != 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
-  const int vpl = ln_vpl(D);
-  if (vpl < 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_final_mask: D=%d above 4096", D);
+  bool wide = false;
+  const int vpl = ln_vpl(D, &wide);
+  if (vpl == 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_final_mask: D=%d above %d", D, kLnWideMaxD);
   if (!x || !gamma || !beta || !out || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
       !aligned16(out) || (reinterpret_cast<uintptr_t>(add16) & 7u) ||
       (reinterpret_cast<uintptr_t>(add16b) & 7u) || (add16b && !add16))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: null or misaligned pointer");
   if (rows == 0) return TJ_OK;
-  const int warps = 8;
-  dim3 grid((rows + warps - 1) / warps);
+  const int per_cta = wide ? 1 : kLnThreads / 32;
+  dim3 grid((rows + per_cta - 1) / per_cta);
   const __half* add = static_cast<const __half*>(add16);
   const __half* addb = static_cast<const __half*>(add16b);
   const int xo = x_at_original ? 1 : 0;
   cudaError_t e = cudaSuccess;
-  switch (vpl) {
-#define TJ_LN_CASE(V) \
-  case V: e = launch_pdl(ln_final_kernel<V>, grid, dim3(warps * 32), 0, stream, x, add, addb, xo, inv_map, rows, D, gamma, beta, eps, out); break;
-    TJ_LN_CASE(1) TJ_LN_CASE(2) TJ_LN_CASE(4) TJ_LN_CASE(8) TJ_LN_CASE(16) TJ_LN_CASE(32)
-#undef TJ_LN_CASE
+#define TJ_LN_CASE(V, R) \
+  e = launch_pdl(ln_final_kernel<V, R>, grid, dim3(kLnThreads), 0, stream, x, add, addb, xo, inv_map, rows, D, gamma, beta, eps, out)
+  if (!wide) {
+    switch (vpl) {
+      case 1: TJ_LN_CASE(1, 32); break;
+      case 2: TJ_LN_CASE(2, 32); break;
+      case 4: TJ_LN_CASE(4, 32); break;
+      case 8: TJ_LN_CASE(8, 32); break;
+      case 16: TJ_LN_CASE(16, 32); break;
+      default: TJ_LN_CASE(32, 32); break;
+    }
+  } else {
+    switch (vpl) {
+      case 8: TJ_LN_CASE(8, kLnThreads); break;
+      case 16: TJ_LN_CASE(16, kLnThreads); break;
+      default: TJ_LN_CASE(32, kLnThreads); break;
+    }
   }
+#undef TJ_LN_CASE
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_final_mask launch: %s", cudaGetErrorString(e));
   return TJ_OK;

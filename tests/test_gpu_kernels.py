@@ -65,7 +65,10 @@ def test_token_plan(cuda_pkg, B, S):
     assert torch.equal(orig, torch.arange(B * S, dtype=torch.int32))
 
 
-@pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (1000, 768), (513, 1024), (64, 4096)])
+# D above 4096 runs a CTA per row (4100: 8 groups per thread, the last partly
+# used; 12288: 16; 32768: 32, the widest row).
+@pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (1000, 768), (513, 1024), (64, 4096),
+                                    (40, 4100), (33, 8192), (20, 12288), (9, 32768)])
 def test_ln_cast_and_final(cuda_pkg, rows, D):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(rows + D)
@@ -93,7 +96,19 @@ def test_ln_cast_and_final(cuda_pkg, rows, D):
     assert torch.count_nonzero(out[~valid]) == 0
 
 
-@pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (513, 1024), (64, 4096)])
+def test_ln_rejects_rows_above_32768(cuda_pkg):
+    k = cuda_pkg.kernels
+    D = 32772
+    x = torch.zeros(2, D, device=DEV)
+    gamma, beta = torch.ones(D, device=DEV), torch.zeros(D, device=DEV)
+    with pytest.raises(RuntimeError, match="above 32768"):
+        k.ln_cast_f16(x, gamma, beta)
+    with pytest.raises(RuntimeError, match="above 32768"):
+        k.ln_final_mask(x, gamma, beta)
+
+
+@pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (513, 1024), (64, 4096), (17, 8192),
+                                    (9, 32768)])
 def test_add_ln_cast_and_final(cuda_pkg, rows, D):
     """Residual add (fp32 x + fp16 branch output) fused into the LayerNorm."""
     k = cuda_pkg.kernels
@@ -127,12 +142,13 @@ def test_add_ln_cast_and_final(cuda_pkg, rows, D):
 
 
 @pytest.mark.parametrize("x_at_original", [True, False])
-def test_add2_ln_final(cuda_pkg, x_at_original):
+@pytest.mark.parametrize("D", [1024, 6144])
+def test_add2_ln_final(cuda_pkg, x_at_original, D):
     """The last layer's two residual adds fused with the final LayerNorm and the
     scatter: LN((x + attn) + ffn), x read at the output row or the compact row."""
     k = cuda_pkg.kernels
-    g = torch.Generator().manual_seed(3 + int(x_at_original))
-    rows, D = 700, 1024
+    g = torch.Generator().manual_seed(3 + int(x_at_original) + D)
+    rows = 700
     inv = torch.full((rows,), -1, dtype=torch.int32)
     valid = torch.randperm(rows, generator=g)[:500].sort().values
     inv[valid] = torch.arange(500, dtype=torch.int32)
@@ -291,6 +307,41 @@ def test_flash_attention_compact(cuda_pkg, lengths, H, causal):
     n = int(cu[-1])
     err = (out[:n].float() - ref[:n]).abs()
     assert torch.isfinite(out[:n].float()).all()
+    assert float(err.max()) < 4e-3, float(err.max())
+
+
+@pytest.mark.parametrize("pattern", ["growing", "spike"])
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_attention_rising_max(cuda_pkg, pattern, causal):
+    """Scores whose row max rises by far more than fp16 can absorb across key
+    tiles (growing key norms), or jumps by ~100 in one key (a spike): the
+    kernel must raise its running max and rescale, whichever way it finds out."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(5 + causal)
+    lengths = [1500, 700, 300]
+    H = 2
+    lens = torch.tensor(lengths, dtype=torch.int32)
+    cu = torch.zeros(len(lengths) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    rows = int(cu[-1])
+    qkv = torch.randn(3, H, rows, 64, generator=g)
+    for b in range(len(lengths)):
+        q0, q1 = int(cu[b]), int(cu[b + 1])
+        pos = torch.arange(q1 - q0, dtype=torch.float32)
+        if pattern == "growing":
+            qkv[1, :, q0:q1] *= (0.2 + 6.0 * pos / (q1 - q0))[None, :, None]
+        else:
+            qkv[1, :, q0 + (q1 - q0) * 3 // 5] = 40.0
+    qkv = qkv.half().to(DEV)
+    q, kk, vv = qkv[0], qkv[1:2], qkv[2:3]
+    kv_off = cu[:-1].view(-1, 1).contiguous()
+    kv_len = lens.view(-1, 1).contiguous()
+    scale = 64**-0.5
+    out = k.flash_attn_fwd(q, kk, vv, cu.to(DEV), kv_off.to(DEV), kv_len.to(DEV), max(lengths), scale,
+                           causal=causal)
+    ref = _attn_ref(q, kk, vv, cu, kv_off, kv_len, scale, causal)
+    err = (out.float() - ref).abs()
+    assert torch.isfinite(out.float()).all()
     assert float(err.max()) < 4e-3, float(err.max())
 
 

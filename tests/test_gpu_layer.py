@@ -148,6 +148,15 @@ def test_large_head_dims(cuda_pkg, cfg_t, pad):
     _gate(oracle.encoder_forward(sd, cfg, x, mask), out, f"{cfg_t}")
 
 
+def test_wide_model(cuda_pkg):
+    """d_model above 4096: the LayerNorms run a CTA per row."""
+    cfg = oracle.TransformerConfig(2, 96, 5120, 40, 512, 1, False)
+    sd = oracle.make_state_dict(cfg, seed=23)
+    x, mask = oracle.generate_random_case(cfg, seed=23, padding_ratio=0.4)
+    out = _run(_model(cuda_pkg, cfg, sd), x, mask)
+    _gate(oracle.encoder_forward(sd, cfg, x, mask), out, "d_model 5120")
+
+
 def test_two_layers_causal(cuda_pkg):
     cfg = oracle.TransformerConfig(2, 640, 256, 4, 1024, 2, True)
     sd = oracle.make_state_dict(cfg, seed=21)
@@ -176,6 +185,12 @@ def test_rejects_unsupported_inputs(cuda_pkg):
     model.train()
     with pytest.raises(RuntimeError):
         model(torch.zeros(1, 128, 256, device=DEV))
+    # fp16 GEMM operand rows must be whole 16-byte units: d_model 100 is refused
+    # before any kernel runs.
+    cfg = oracle.TransformerConfig(1, 16, 100, 4, 64, 1, False)
+    model = _model(cuda_pkg, cfg, oracle.make_state_dict(cfg, seed=1))
+    with pytest.raises(RuntimeError, match="multiples of 8"):
+        model(torch.zeros(1, 16, 100, device=DEV))
 
 
 def test_cuda_graph_replay_matches_eager(cuda_pkg):
