@@ -210,18 +210,21 @@ typedef struct tj_encoder_desc {
   float ln_eps;
 } tj_encoder_desc;
 
+/* fp16 weights are [N, K] row-major with rows padded to K8 = K rounded up
+ * to a multiple of 8 columns (K8 = K when K is a multiple of 8); the padding
+ * columns are never read. */
 typedef struct tj_layer_weights {
   const float* ln1_gamma;   /* norm1.weight [D] */
   const float* ln1_beta;    /* norm1.bias [D] */
-  const void* w_qkv16;      /* cat(q,k,v)_proj.weight as fp16 [3D, D] */
+  const void* w_qkv16;      /* cat(q,k,v)_proj.weight as fp16 [3D, D8] */
   const float* b_qkv;       /* cat(q,k,v)_proj.bias [3D] */
-  const void* w_out16;      /* attention.out_proj.weight fp16 [D, D] */
+  const void* w_out16;      /* attention.out_proj.weight fp16 [D, D8] */
   const float* b_out;       /* [D] */
   const float* ln2_gamma;   /* norm2.weight */
   const float* ln2_beta;
-  const void* w_ffn_in16;   /* ffn_in.weight fp16 [F, D] */
+  const void* w_ffn_in16;   /* ffn_in.weight fp16 [F, D8] */
   const float* b_ffn_in;    /* [F] */
-  const void* w_ffn_out16;  /* ffn_out.weight fp16 [D, F] */
+  const void* w_ffn_out16;  /* ffn_out.weight fp16 [D, F8] */
   const float* b_ffn_out;   /* [D] */
 } tj_layer_weights;
 

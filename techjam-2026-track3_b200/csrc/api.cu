@@ -76,12 +76,13 @@ static bool workspace_layout(const tj_encoder_desc* d, EncoderWorkspace* w) {
       d->ffn_dim <= 0 || d->num_layers <= 0 || d->d_model % d->num_heads != 0)
     return false;
   const size_t rows = (size_t)d->batch * d->seq_len;
-  const size_t D = d->d_model, F = d->ffn_dim;
+  // fp16 rows padded to a multiple of 8 columns (16-byte TMA rows).
+  const size_t D = d->d_model, F = d->ffn_dim, D8 = align_up(D, 8), F8 = align_up(F, 8);
   size_t off = 0;
   w->plan = off;
   off = align_up(off + (size_t)plan_ints(d->batch, d->seq_len) * 4, 256);
   w->a16 = off;
-  off = align_up(off + rows * D * 2, 256);
+  off = align_up(off + rows * D8 * 2, 256);
   w->qkv16 = off;  // head-major [3][H][rows][P], heads zero-padded to P = 64, 128 or 256
   off = align_up(off + 3 * rows * (size_t)d->num_heads * attn_head_pad(d->d_model / d->num_heads) * 2, 256);
   w->x1 = off;
@@ -89,11 +90,11 @@ static bool workspace_layout(const tj_encoder_desc* d, EncoderWorkspace* w) {
   w->x2 = off;
   off = align_up(off + rows * D * 4, 256);
   w->h16 = off;
-  off = align_up(off + rows * F * 2, 256);
+  off = align_up(off + rows * F8 * 2, 256);
   w->y16 = off;  // fp16 output of the out-projection / FFN-out before its residual add
-  off = align_up(off + rows * D * 2, 256);
+  off = align_up(off + rows * D8 * 2, 256);
   w->y16b = off;  // the last layer's FFN-out (its out-projection output stays in y16)
-  off = align_up(off + rows * D * 2, 256);
+  off = align_up(off + rows * D8 * 2, 256);
   w->total = off;
   return true;
 }
@@ -357,11 +358,11 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
   const int dh = D / H;
   if (dh > 256)
     return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: head_dim %d (1..256 supported)", dh);
-  // fp16 GEMM operand rows must be whole 16-byte units for their TMA loads.
-  if (D % 8 != 0 || F % 8 != 0)
-    return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: d_model %d and ffn_dim %d must be multiples of 8", D, F);
-  if (D > 32768)
-    return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: d_model %d above 32768", D);
+  if (D > (D % 4 == 0 ? 32768 : 8192))
+    return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: d_model %d above %d", D, D % 4 == 0 ? 32768 : 8192);
+  // fp16 activations and weights have rows padded to a multiple of 8 columns,
+  // whole 16-byte units for the GEMMs' TMA loads (which stop at the true K).
+  const int D8 = (D + 7) / 8 * 8, F8 = (F + 7) / 8 * 8;
   const int kPad = attn_head_pad(dh);  // head-major row length of the QKV buffer
   if ((int64_t)B * S > INT32_MAX / 4)
     return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: B*S too large");
@@ -393,10 +394,11 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     const float* xin = (l == 0) ? x : x2;
     const int32_t* in_map = (l == 0) ? plan.orig() : nullptr;
     if (l == 0)
-      rc = launch_ln_cast_f16(x, in_map, nv, rows, D, L.ln1_gamma, L.ln1_beta, d->ln_eps, a16, s);
+      rc = launch_ln_cast_f16(x, in_map, nv, rows, D, L.ln1_gamma, L.ln1_beta, d->ln_eps, a16, s, nullptr,
+                              nullptr, D8, D8);
     else  // x2 = x1 + FFN-out of the previous layer
       rc = launch_ln_cast_f16(x1, nullptr, nv, rows, D, L.ln1_gamma, L.ln1_beta, d->ln_eps, a16, s,
-                              y16, x2);
+                              y16, x2, D8, D8);
     if (rc) return rc;
     GemmArgs g{};
     g.a16 = a16;
@@ -406,6 +408,7 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     g.rows_max = rows;
     g.N = 3 * D;
     g.K = D;
+    g.lda = g.ldw = D8;
     g.out = qkv16;
     g.heads = H;
     g.head_dim = dh;
@@ -433,6 +436,7 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     a.q_pos0 = nullptr;
     a.order = plan.order();
     a.ctx = a16;  // LN1 output is dead once the QKV GEMM has run
+    a.ld_ctx = D8;
     rc = launch_attention(a, s);
     if (rc) return rc;
     GemmArgs o{};
@@ -443,13 +447,14 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     o.rows_max = rows;
     o.N = D;
     o.K = D;
+    o.lda = o.ldw = D8;
     o.out = y16;
-    o.ld_out = D;
+    o.ld_out = D8;
     rc = launch_gemm(kEpiBiasF16, o, s);
     if (rc) return rc;
     // x1 = x + attention output; a16 = LN2(x1)
     rc = launch_ln_cast_f16(xin, in_map, nv, rows, D, L.ln2_gamma, L.ln2_beta, d->ln_eps, a16, s, y16,
-                            last ? nullptr : x1);
+                            last ? nullptr : x1, D8, D8);
     if (rc) return rc;
     GemmArgs f1{};
     f1.a16 = a16;
@@ -459,8 +464,9 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     f1.rows_max = rows;
     f1.N = F;
     f1.K = D;
+    f1.lda = f1.ldw = D8;
     f1.out = h16;
-    f1.ld_out = F;
+    f1.ld_out = F8;
     rc = launch_gemm(kEpiGeluF16, f1, s);
     if (rc) return rc;
     GemmArgs f2{};
@@ -471,8 +477,9 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     f2.rows_max = rows;
     f2.N = D;
     f2.K = F;
+    f2.lda = f2.ldw = F8;
     f2.out = last ? y16b : y16;
-    f2.ld_out = D;
+    f2.ld_out = D8;
     rc = launch_gemm(kEpiBiasF16, f2, s);
     if (rc) return rc;
   }
@@ -481,7 +488,7 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
   // at the output row) or the last layer's compact input x2.
   const bool one_layer = d->num_layers == 1;
   rc = launch_ln_final(one_layer ? x : x2, plan.inv(), rows, D, final_gamma, final_beta, d->ln_eps, out,
-                       s, y16, y16b, one_layer);
+                       s, y16, y16b, one_layer, D8);
   return finish(rc, s);
 }
 

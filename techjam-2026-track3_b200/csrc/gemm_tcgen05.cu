@@ -225,9 +225,15 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
       for (int g = 0; g < 4; ++g) {
         const int n = nc + 8 * g;
         float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
-        if (n < p.N) {
+        if (n + 8 <= p.N) {
           b0 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
           b1 = __ldg(reinterpret_cast<const float4*>(p.bias + n) + 1);
+        } else if (n < p.N) {  // last, partial group of an N that is not a multiple of 8
+          float bb[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) bb[e] = n + e < p.N ? __ldg(p.bias + n + e) : 0.f;
+          b0 = make_float4(bb[0], bb[1], bb[2], bb[3]);
+          b1 = make_float4(bb[4], bb[5], bb[6], bb[7]);
         }
         float2 w[4] = {make_float2(__uint_as_float(r[8 * g + 0]) + b0.x, __uint_as_float(r[8 * g + 1]) + b0.y),
                        make_float2(__uint_as_float(r[8 * g + 2]) + b0.z, __uint_as_float(r[8 * g + 3]) + b0.w),
@@ -264,6 +270,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const int ne = n + e;
+                if (ne >= p.N) break;
                 const int which = ne / p.d_model;
                 const int rem = ne - which * p.d_model;
                 const int h = rem / p.head_dim;
@@ -727,12 +734,12 @@ static int launch_gemm_t(const GemmArgs& a, const GemmKernelParams& kp, cudaStre
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta, tb;
   uint64_t da[2] = {(uint64_t)a.K, (uint64_t)a.rows_max};
-  uint64_t sa[1] = {(uint64_t)a.K};
+  uint64_t sa[1] = {(uint64_t)a.lda};
   uint32_t ba[2] = {kBK, kBM};
   int rc = make_tmap_f16(&ta, a.a16, 2, da, sa, ba);
   if (rc) return rc;
   uint64_t db[2] = {(uint64_t)a.K, (uint64_t)a.N};
-  uint64_t sb[1] = {(uint64_t)a.K};
+  uint64_t sb[1] = {(uint64_t)a.ldw};
   uint32_t bb[2] = {kBK, (uint32_t)BN};
   rc = make_tmap_f16(&tb, a.w16, 2, db, sb, bb);
   if (rc) return rc;
@@ -804,12 +811,12 @@ static int launch_gemm_pair(const GemmArgs& a, const GemmKernelParams& kp, int c
                             cudaStream_t stream) {
   CUtensorMap ta, tb;
   uint64_t da[2] = {(uint64_t)a.K, (uint64_t)a.rows_max};
-  uint64_t sa[1] = {(uint64_t)a.K};
+  uint64_t sa[1] = {(uint64_t)a.lda};
   uint32_t ba[2] = {kBK, kBM};
   int rc = make_tmap_f16(&ta, a.a16, 2, da, sa, ba);
   if (rc) return rc;
   uint64_t db[2] = {(uint64_t)a.K, (uint64_t)a.N};
-  uint64_t sb[1] = {(uint64_t)a.K};
+  uint64_t sb[1] = {(uint64_t)a.ldw};
   uint32_t bb[2] = {kBK, (uint32_t)(PairCfg::kBN / 2)};
   rc = make_tmap_f16(&tb, a.w16, 2, db, sb, bb);
   if (rc) return rc;
@@ -838,11 +845,18 @@ static int launch_gemm_bn(const GemmArgs& a, const GemmKernelParams& kp, cudaStr
   return launch_gemm_t<256, EPI>(a, kp, stream);
 }
 
-int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
+int launch_gemm(int epilogue, const GemmArgs& args, cudaStream_t stream) {
+  GemmArgs a = args;
+  if (a.lda <= 0) a.lda = a.K;
+  if (a.ldw <= 0) a.ldw = a.K;
   if (a.rows_max < 0 || a.N <= 0 || a.K <= 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: rows=%d N=%d K=%d", a.rows_max, a.N, a.K);
-  if (a.K % 8 != 0 || a.N % 8 != 0)
-    return set_error(TJ_ERR_UNSUPPORTED, "gemm: N=%d and K=%d must be multiples of 8", a.N, a.K);
+  // TMA rows are whole 16-byte units; a K that is not a multiple of 8 is read
+  // through padded row strides (the tile loads zero-fill past K).
+  if (a.lda < a.K || a.ldw < a.K || a.lda % 8 != 0 || a.ldw % 8 != 0)
+    return set_error(TJ_ERR_UNSUPPORTED,
+                     "gemm: K=%d needs row strides that are multiples of 8 and >= K (lda=%d ldw=%d)", a.K,
+                     a.lda, a.ldw);
   if (!a.a16 || !a.w16 || !a.bias || !a.out)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: null pointer");
   if ((reinterpret_cast<uintptr_t>(a.a16) | reinterpret_cast<uintptr_t>(a.w16) |
@@ -872,17 +886,23 @@ int launch_gemm(int epilogue, const GemmArgs& a, cudaStream_t stream) {
       kp.head_pad = attn_head_pad(a.head_dim);
       return launch_gemm_bn<kEpiQkvHeadMajor>(a, kp, stream);
     case kEpiResidualF32:
+      if (a.N % 8 != 0)
+        return set_error(TJ_ERR_UNSUPPORTED, "gemm_bias_residual_f32: N=%d must be a multiple of 8", a.N);
       if (!a.resid || (reinterpret_cast<uintptr_t>(a.resid) & 15u) || a.ld_resid % 4 != 0 ||
           a.ld_out % 4 != 0)
         return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_residual_f32: residual must be 16-byte aligned");
       return launch_gemm_bn<kEpiResidualF32>(a, kp, stream);
+    // The fp16 epilogues store 8 columns at a time: a last partial group
+    // writes zeros into the row padding, so the row stride must cover it.
     case kEpiGeluF16:
-      if (a.ld_out % 8 != 0)
-        return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_gelu_f16: ld_out must be a multiple of 8");
+      if (a.ld_out % 8 != 0 || a.ld_out < (a.N + 7) / 8 * 8)
+        return set_error(TJ_ERR_INVALID_ARGUMENT,
+                         "gemm_bias_gelu_f16: ld_out=%d must be a multiple of 8 covering N=%d", a.ld_out, a.N);
       return launch_gemm_bn<kEpiGeluF16>(a, kp, stream);
     case kEpiBiasF16:
-      if (a.ld_out % 8 != 0)
-        return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm_bias_f16: ld_out must be a multiple of 8");
+      if (a.ld_out % 8 != 0 || a.ld_out < (a.N + 7) / 8 * 8)
+        return set_error(TJ_ERR_INVALID_ARGUMENT,
+                         "gemm_bias_f16: ld_out=%d must be a multiple of 8 covering N=%d", a.ld_out, a.N);
       return launch_gemm_bn<kEpiBiasF16>(a, kp, stream);
     default:
       return set_error(TJ_ERR_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epilogue);

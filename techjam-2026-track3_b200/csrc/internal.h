@@ -66,17 +66,20 @@ struct PlanView {
 int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStream_t stream);
 
 // add16 (optional, fp16, compact rows) is added to the x row before the
-// LayerNorm; sum_out (optional) receives that fp32 sum.
+// LayerNorm; sum_out (optional) receives that fp32 sum.  fp32 rows have
+// stride D; ld_y / ld_add are the fp16 row strides (0 = D).
 int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* row_count, int rows,
                        int D, const float* gamma, const float* beta, float eps, void* y16,
-                       cudaStream_t stream, const void* add16 = nullptr, float* sum_out = nullptr);
+                       cudaStream_t stream, const void* add16 = nullptr, float* sum_out = nullptr,
+                       int ld_y = 0, int ld_add = 0);
 
 // add16b (optional) is a second fp16 addend; with x_at_original, x is read
-// at the output row m instead of the compact row inv_map[m].
+// at the output row m instead of the compact row inv_map[m].  ld_add is the
+// fp16 addends' row stride (0 = D).
 int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
                     const float* beta, float eps, float* out, cudaStream_t stream,
                     const void* add16 = nullptr, const void* add16b = nullptr,
-                    bool x_at_original = false);
+                    bool x_at_original = false, int ld_add = 0);
 
 enum GemmEpilogue : int {
   kEpiQkvHeadMajor = 0,   // fp16 out, head-major [3][H][rows_max][attn_head_pad(dh)]
@@ -86,11 +89,12 @@ enum GemmEpilogue : int {
 };
 
 struct GemmArgs {
-  const void* a16;          // [rows_max, K] fp16, row-major
-  const void* w16;          // [N, K] fp16, row-major (nn.Linear layout)
+  const void* a16;          // [rows_max, K] fp16, row stride lda
+  const void* w16;          // [N, K] fp16, row stride ldw (nn.Linear layout)
   const float* bias;        // [N]
   const int32_t* row_count; // device int (rows actually present), or null = rows_max
   int rows_max, N, K;
+  int lda, ldw;             // row strides in elements, multiples of 8 (0 = K)
   void* out;                // epilogue-dependent
   int ld_out;               // elements
   const float* resid;       // kEpiResidualF32

@@ -158,10 +158,13 @@ int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStre
 }
 
 // ---------------------------------------------------------------------------
-// LayerNorm.  RT threads per row: one warp (RT = 32, D <= 4096) or a whole
-// CTA of 256 threads (RT = 256, wider rows up to 32768).  Thread k of a row
-// holds float4 groups k, k+RT, ... (VPL groups, so D <= 4 * RT * VPL), and
-// the row stays in registers between the mean and the variance pass.
+// LayerNorm.  RT threads per row: one warp (RT = 32) or a whole CTA of 256
+// threads (RT = 256) for wide rows.  A row is cut into groups of VW columns
+// (4: float4 loads; 1 when D is not a multiple of 4); thread k of a row holds
+// groups k, k+RT, ... (VPL of them, so D <= VW * RT * VPL), and the row stays
+// in registers between the mean and the variance pass.  fp32 rows have stride
+// D; fp16 rows (outputs and addends) their own stride, which the encoder pads
+// to a multiple of 8 for the GEMMs' 16-byte TMA rows.
 // ---------------------------------------------------------------------------
 constexpr int kLnThreads = 256;
 constexpr int kLnWideMaxD = 4 * kLnThreads * 32;
@@ -185,54 +188,74 @@ __device__ __forceinline__ float ln_row_sum(float s, float* red) {
   return s;
 }
 
-template <int VPL, int RT>
-__device__ __forceinline__ void ln_row_stats(const float4 (&v)[VPL], int D, int k, float& mean,
+template <int VW>
+__device__ __forceinline__ void ln_load(const float* row, int g, float (&v)[VW]) {
+  if constexpr (VW == 4) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(row) + g);
+    v[0] = t.x;
+    v[1] = t.y;
+    v[2] = t.z;
+    v[3] = t.w;
+  } else {
+    v[0] = __ldg(row + g);
+  }
+}
+
+template <int VW>
+__device__ __forceinline__ void ln_store(float* row, int g, const float (&v)[VW]) {
+  if constexpr (VW == 4)
+    reinterpret_cast<float4*>(row)[g] = make_float4(v[0], v[1], v[2], v[3]);
+  else
+    row[g] = v[0];
+}
+
+// v += the VW fp16 values of group g of an addend row (fp32 sum).
+template <int VW>
+__device__ __forceinline__ void ln_add_f16(const __half* row, int g, float (&v)[VW]) {
+  if constexpr (VW == 4) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(row) + g);
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    v[0] += lo.x;
+    v[1] += lo.y;
+    v[2] += hi.x;
+    v[3] += hi.y;
+  } else {
+    v[0] += __half2float(row[g]);
+  }
+}
+
+template <int VPL, int RT, int VW>
+__device__ __forceinline__ void ln_row_stats(const float (&v)[VPL][VW], int D, int k, float& mean,
                                              float& rstd, float eps, float* red) {
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    if ((i * RT + k) * 4 < D) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  }
+  for (int i = 0; i < VPL; ++i)
+    if ((i * RT + k) * VW < D)
+#pragma unroll
+      for (int e = 0; e < VW; ++e) s += v[i][e];
   mean = ln_row_sum<RT>(s, red) / (float)D;
   float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    if ((i * RT + k) * 4 < D) {
-      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-      q += (a * a + b * b) + (c * c + d * d);
-    }
-  }
-  rstd = 1.0f / sqrtf(ln_row_sum<RT>(q, red) / (float)D + eps);
-}
-
-// v[i] += the four fp16 values of group g of an addend row (fp32 sum).
-template <int VPL, int RT>
-__device__ __forceinline__ void add_f16_row(float4 (&v)[VPL], const __half* add_row, int D, int k) {
-  const uint2* ar = reinterpret_cast<const uint2*>(add_row);
+  for (int i = 0; i < VPL; ++i)
+    if ((i * RT + k) * VW < D)
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int g = i * RT + k;
-    if (g * 4 < D) {
-      const uint2 u = __ldg(ar + g);
-      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-      v[i].x += lo.x;
-      v[i].y += lo.y;
-      v[i].z += hi.x;
-      v[i].w += hi.y;
-    }
-  }
+      for (int e = 0; e < VW; ++e) {
+        const float c = v[i][e] - mean;
+        q += c * c;
+      }
+  rstd = 1.0f / sqrtf(ln_row_sum<RT>(q, red) / (float)D + eps);
 }
 
 // y[r] = fp16(LayerNorm(x[row_map[r]] (+ add16[r]))), and with sum_out the
 // fp32 row x[row_map[r]] + add16[r] is stored to sum_out[r] (the residual
 // stream after a branch whose output the GEMM left in fp16).
-template <int VPL, int RT>
+template <int VPL, int RT, int VW>
 __global__ void __launch_bounds__(kLnThreads) ln_cast_f16_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ row_map,
-    const __half* __restrict__ add16, const int32_t* __restrict__ row_count, int rows, int D,
-    const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
-    float* __restrict__ sum_out, __half* __restrict__ y) {
+    const __half* __restrict__ add16, int ld_add, const int32_t* __restrict__ row_count, int rows,
+    int D, const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+    float* __restrict__ sum_out, __half* __restrict__ y, int ld_y) {
   __shared__ float red[kLnThreads / 32];
   const int k = (int)threadIdx.x % RT;
   const int row = blockIdx.x * (kLnThreads / RT) + (int)threadIdx.x / RT;
@@ -241,46 +264,49 @@ __global__ void __launch_bounds__(kLnThreads) ln_cast_f16_kernel(
   const int limit = row_count ? min(rows, *row_count) : rows;
   if (row >= limit) return;  // uniform for the RT threads of a row
   const int64_t src = row_map ? (int64_t)row_map[row] : (int64_t)row;
-  const float4* xr = reinterpret_cast<const float4*>(x + src * D);
-  float4 v[VPL];
+  const float* xr = x + src * D;
+  float v[VPL][VW];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int g = i * RT + k;
-    v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  if (add16) add_f16_row<VPL, RT>(v, add16 + (int64_t)row * D, D, k);
-  if (sum_out) {
-    float4* sr = reinterpret_cast<float4*>(sum_out + (int64_t)row * D);
+    if (g * VW < D) {
+      ln_load<VW>(xr, g, v[i]);
+      if (add16) ln_add_f16<VW>(add16 + (int64_t)row * ld_add, g, v[i]);
+      if (sum_out) ln_store<VW>(sum_out + (int64_t)row * D, g, v[i]);
+    } else {
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int g = i * RT + k;
-      if (g * 4 < D) sr[g] = v[i];
+      for (int e = 0; e < VW; ++e) v[i][e] = 0.f;
     }
   }
   float mean, rstd;
-  ln_row_stats<VPL, RT>(v, D, k, mean, rstd, eps, red);
-  uint2* yr = reinterpret_cast<uint2*>(y + (int64_t)row * D);
+  ln_row_stats<VPL, RT, VW>(v, D, k, mean, rstd, eps, red);
+  __half* yr = y + (int64_t)row * ld_y;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int g = i * RT + k;
-    if (g * 4 < D) {
-      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma) + g);
-      const float4 be = __ldg(reinterpret_cast<const float4*>(beta) + g);
-      uint2 o;
-      o.x = pack_half2((v[i].x - mean) * rstd * ga.x + be.x, (v[i].y - mean) * rstd * ga.y + be.y);
-      o.y = pack_half2((v[i].z - mean) * rstd * ga.z + be.z, (v[i].w - mean) * rstd * ga.w + be.w);
-      yr[g] = o;
+    if (g * VW < D) {
+      float ga[VW], be[VW];
+      ln_load<VW>(gamma, g, ga);
+      ln_load<VW>(beta, g, be);
+      if constexpr (VW == 4) {
+        uint2 o;
+        o.x = pack_half2((v[i][0] - mean) * rstd * ga[0] + be[0], (v[i][1] - mean) * rstd * ga[1] + be[1]);
+        o.y = pack_half2((v[i][2] - mean) * rstd * ga[2] + be[2], (v[i][3] - mean) * rstd * ga[3] + be[3]);
+        reinterpret_cast<uint2*>(yr)[g] = o;
+      } else {
+        yr[g] = __float2half_rn((v[i][0] - mean) * rstd * ga[0] + be[0]);
+      }
     }
   }
 }
 
 // out[m] = LayerNorm(x + add16[c] (+ add16b[c])) for c = inv_map[m] >= 0 (x
 // read at row c, or at row m with x_at_original), exact zeros otherwise.
-template <int VPL, int RT>
+template <int VPL, int RT, int VW>
 __global__ void __launch_bounds__(kLnThreads) ln_final_kernel(const float* __restrict__ x,
                                                               const __half* __restrict__ add16,
                                                               const __half* __restrict__ add16b,
-                                                              int x_at_original,
+                                                              int ld_add, int x_at_original,
                                                               const int32_t* __restrict__ inv_map,
                                                               int rows, int D,
                                                               const float* __restrict__ gamma,
@@ -293,47 +319,51 @@ __global__ void __launch_bounds__(kLnThreads) ln_final_kernel(const float* __res
   pdl_trigger();
   if (row >= rows) return;  // uniform for the RT threads of a row
   const int64_t src = inv_map ? (int64_t)inv_map[row] : (int64_t)row;
-  float4* orow = reinterpret_cast<float4*>(out + (int64_t)row * D);
+  float* orow = out + (int64_t)row * D;
   if (src < 0) {  // padded token: exact zero, as masked_fill(~mask, 0) gives
+    const float z[VW] = {};
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int g = i * RT + k;
-      if (g * 4 < D) orow[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (g * VW < D) ln_store<VW>(orow, g, z);
     }
     return;
   }
-  const float4* xr = reinterpret_cast<const float4*>(x + (x_at_original ? (int64_t)row : src) * D);
-  float4 v[VPL];
+  const float* xr = x + (x_at_original ? (int64_t)row : src) * D;
+  float v[VPL][VW];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int g = i * RT + k;
-    v[i] = (g * 4 < D) ? __ldg(xr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g * VW < D) {
+      ln_load<VW>(xr, g, v[i]);
+      if (add16) ln_add_f16<VW>(add16 + src * ld_add, g, v[i]);
+      if (add16b) ln_add_f16<VW>(add16b + src * ld_add, g, v[i]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VW; ++e) v[i][e] = 0.f;
+    }
   }
-  if (add16) add_f16_row<VPL, RT>(v, add16 + src * D, D, k);
-  if (add16b) add_f16_row<VPL, RT>(v, add16b + src * D, D, k);
   float mean, rstd;
-  ln_row_stats<VPL, RT>(v, D, k, mean, rstd, eps, red);
+  ln_row_stats<VPL, RT, VW>(v, D, k, mean, rstd, eps, red);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int g = i * RT + k;
-    if (g * 4 < D) {
-      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma) + g);
-      const float4 be = __ldg(reinterpret_cast<const float4*>(beta) + g);
-      float4 o;
-      o.x = (v[i].x - mean) * rstd * ga.x + be.x;
-      o.y = (v[i].y - mean) * rstd * ga.y + be.y;
-      o.z = (v[i].z - mean) * rstd * ga.z + be.z;
-      o.w = (v[i].w - mean) * rstd * ga.w + be.w;
-      orow[g] = o;
+    if (g * VW < D) {
+      float ga[VW], be[VW], o[VW];
+      ln_load<VW>(gamma, g, ga);
+      ln_load<VW>(beta, g, be);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) o[e] = (v[i][e] - mean) * rstd * ga[e] + be[e];
+      ln_store<VW>(orow, g, o);
     }
   }
 }
 
-// Groups of 4 columns per thread for a row of D columns: a warp per row up to
-// D = 4096 (VPL 1..32), then a CTA per row (VPL 8, 16, 32 of 256 threads).
-// Returns 0 when D is above kLnWideMaxD.
-static int ln_vpl(int D, bool* wide) {
-  const int groups = D / 4;
+// Groups per thread for a row of D columns in groups of VW: a warp per row up
+// to 32 * 32 groups (VPL 1..32), then a CTA per row (VPL 8, 16, 32 of 256
+// threads).  Returns 0 when the row is wider than that.
+static int ln_vpl(int D, int VW, bool* wide) {
+  const int groups = D / VW;
   *wide = groups > 32 * 32;
   const int per = *wide ? (groups + kLnThreads - 1) / kLnThreads : (groups + 31) / 32;
   for (int v = 1; v <= 32; v *= 2)
@@ -345,15 +375,24 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* row_count, int rows,
                        int D, const float* gamma, const float* beta, float eps, void* y16,
-                       cudaStream_t stream, const void* add16, float* sum_out) {
-  if (rows < 0 || D <= 0 || D % 4 != 0)
-    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
+                       cudaStream_t stream, const void* add16, float* sum_out, int ld_y, int ld_add) {
+  if (ld_y <= 0) ld_y = D;
+  if (ld_add <= 0) ld_add = D;
+  if (rows < 0 || D <= 0 || ld_y < D || ld_add < D)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: rows=%d D=%d ld_y=%d ld_add=%d", rows, D, ld_y, ld_add);
+  // float4 groups need 16-byte fp32 rows and 8-byte fp16 rows.
+  const int VW = (D % 4 == 0 && ld_y % 4 == 0 && ld_add % 4 == 0 && aligned16(x) && aligned16(gamma) &&
+                  aligned16(beta) && aligned16(sum_out) && (reinterpret_cast<uintptr_t>(y16) & 7u) == 0 &&
+                  (reinterpret_cast<uintptr_t>(add16) & 7u) == 0)
+                     ? 4 : 1;
   bool wide = false;
-  const int vpl = ln_vpl(D, &wide);
-  if (vpl == 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_cast_f16: D=%d above %d", D, kLnWideMaxD);
-  if (!x || !gamma || !beta || !y16 || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
-      (reinterpret_cast<uintptr_t>(y16) & 7u) || (reinterpret_cast<uintptr_t>(add16) & 7u) ||
-      !aligned16(sum_out))
+  const int vpl = ln_vpl(D, VW, &wide);
+  if (vpl == 0)
+    return set_error(TJ_ERR_UNSUPPORTED, "ln_cast_f16: D=%d above %d", D, VW == 4 ? kLnWideMaxD : kLnWideMaxD / 4);
+  if (!x || !gamma || !beta || !y16 || (reinterpret_cast<uintptr_t>(x) & 3u) ||
+      (reinterpret_cast<uintptr_t>(gamma) & 3u) || (reinterpret_cast<uintptr_t>(beta) & 3u) ||
+      (reinterpret_cast<uintptr_t>(sum_out) & 3u) || (reinterpret_cast<uintptr_t>(y16) & 1u) ||
+      (reinterpret_cast<uintptr_t>(add16) & 1u))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_cast_f16: null or misaligned pointer");
   if (rows == 0) return TJ_OK;
   const int per_cta = wide ? 1 : kLnThreads / 32;
@@ -361,24 +400,31 @@ int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* ro
   __half* y = static_cast<__half*>(y16);
   const __half* add = static_cast<const __half*>(add16);
   cudaError_t e = cudaSuccess;
-#define TJ_LN_CASE(V, R) \
-  e = launch_pdl(ln_cast_f16_kernel<V, R>, grid, dim3(kLnThreads), 0, stream, x, row_map, add, row_count, rows, D, gamma, beta, eps, sum_out, y)
-  if (!wide) {
-    switch (vpl) {
-      case 1: TJ_LN_CASE(1, 32); break;
-      case 2: TJ_LN_CASE(2, 32); break;
-      case 4: TJ_LN_CASE(4, 32); break;
-      case 8: TJ_LN_CASE(8, 32); break;
-      case 16: TJ_LN_CASE(16, 32); break;
-      default: TJ_LN_CASE(32, 32); break;
-    }
-  } else {
-    switch (vpl) {
-      case 8: TJ_LN_CASE(8, kLnThreads); break;
-      case 16: TJ_LN_CASE(16, kLnThreads); break;
-      default: TJ_LN_CASE(32, kLnThreads); break;
-    }
+#define TJ_LN_CASE(V, R, W) \
+  e = launch_pdl(ln_cast_f16_kernel<V, R, W>, grid, dim3(kLnThreads), 0, stream, x, row_map, add, ld_add, row_count, rows, D, gamma, beta, eps, sum_out, y, ld_y)
+#define TJ_LN_SWITCH(W)                                   \
+  if (!wide) {                                            \
+    switch (vpl) {                                        \
+      case 1: TJ_LN_CASE(1, 32, W); break;                \
+      case 2: TJ_LN_CASE(2, 32, W); break;                \
+      case 4: TJ_LN_CASE(4, 32, W); break;                \
+      case 8: TJ_LN_CASE(8, 32, W); break;                \
+      case 16: TJ_LN_CASE(16, 32, W); break;              \
+      default: TJ_LN_CASE(32, 32, W); break;              \
+    }                                                     \
+  } else {                                                \
+    switch (vpl) {                                        \
+      case 8: TJ_LN_CASE(8, kLnThreads, W); break;        \
+      case 16: TJ_LN_CASE(16, kLnThreads, W); break;      \
+      default: TJ_LN_CASE(32, kLnThreads, W); break;      \
+    }                                                     \
   }
+  if (VW == 4) {
+    TJ_LN_SWITCH(4)
+  } else {
+    TJ_LN_SWITCH(1)
+  }
+#undef TJ_LN_SWITCH
 #undef TJ_LN_CASE
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_cast_f16 launch: %s", cudaGetErrorString(e));
@@ -387,15 +433,22 @@ int launch_ln_cast_f16(const float* x, const int32_t* row_map, const int32_t* ro
 
 int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, const float* gamma,
                     const float* beta, float eps, float* out, cudaStream_t stream,
-                    const void* add16, const void* add16b, bool x_at_original) {
-  if (rows < 0 || D <= 0 || D % 4 != 0)
-    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: rows=%d D=%d (D must be a positive multiple of 4)", rows, D);
+                    const void* add16, const void* add16b, bool x_at_original, int ld_add) {
+  if (ld_add <= 0) ld_add = D;
+  if (rows < 0 || D <= 0 || ld_add < D)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: rows=%d D=%d ld_add=%d", rows, D, ld_add);
+  const int VW = (D % 4 == 0 && ld_add % 4 == 0 && aligned16(x) && aligned16(gamma) && aligned16(beta) &&
+                  aligned16(out) && (reinterpret_cast<uintptr_t>(add16) & 7u) == 0 &&
+                  (reinterpret_cast<uintptr_t>(add16b) & 7u) == 0)
+                     ? 4 : 1;
   bool wide = false;
-  const int vpl = ln_vpl(D, &wide);
-  if (vpl == 0) return set_error(TJ_ERR_UNSUPPORTED, "ln_final_mask: D=%d above %d", D, kLnWideMaxD);
-  if (!x || !gamma || !beta || !out || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) ||
-      !aligned16(out) || (reinterpret_cast<uintptr_t>(add16) & 7u) ||
-      (reinterpret_cast<uintptr_t>(add16b) & 7u) || (add16b && !add16))
+  const int vpl = ln_vpl(D, VW, &wide);
+  if (vpl == 0)
+    return set_error(TJ_ERR_UNSUPPORTED, "ln_final_mask: D=%d above %d", D, VW == 4 ? kLnWideMaxD : kLnWideMaxD / 4);
+  if (!x || !gamma || !beta || !out || (reinterpret_cast<uintptr_t>(x) & 3u) ||
+      (reinterpret_cast<uintptr_t>(gamma) & 3u) || (reinterpret_cast<uintptr_t>(beta) & 3u) ||
+      (reinterpret_cast<uintptr_t>(out) & 3u) || (reinterpret_cast<uintptr_t>(add16) & 1u) ||
+      (reinterpret_cast<uintptr_t>(add16b) & 1u) || (add16b && !add16))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "ln_final_mask: null or misaligned pointer");
   if (rows == 0) return TJ_OK;
   const int per_cta = wide ? 1 : kLnThreads / 32;
@@ -404,24 +457,31 @@ int launch_ln_final(const float* x, const int32_t* inv_map, int rows, int D, con
   const __half* addb = static_cast<const __half*>(add16b);
   const int xo = x_at_original ? 1 : 0;
   cudaError_t e = cudaSuccess;
-#define TJ_LN_CASE(V, R) \
-  e = launch_pdl(ln_final_kernel<V, R>, grid, dim3(kLnThreads), 0, stream, x, add, addb, xo, inv_map, rows, D, gamma, beta, eps, out)
-  if (!wide) {
-    switch (vpl) {
-      case 1: TJ_LN_CASE(1, 32); break;
-      case 2: TJ_LN_CASE(2, 32); break;
-      case 4: TJ_LN_CASE(4, 32); break;
-      case 8: TJ_LN_CASE(8, 32); break;
-      case 16: TJ_LN_CASE(16, 32); break;
-      default: TJ_LN_CASE(32, 32); break;
-    }
-  } else {
-    switch (vpl) {
-      case 8: TJ_LN_CASE(8, kLnThreads); break;
-      case 16: TJ_LN_CASE(16, kLnThreads); break;
-      default: TJ_LN_CASE(32, kLnThreads); break;
-    }
+#define TJ_LN_CASE(V, R, W) \
+  e = launch_pdl(ln_final_kernel<V, R, W>, grid, dim3(kLnThreads), 0, stream, x, add, addb, ld_add, xo, inv_map, rows, D, gamma, beta, eps, out)
+#define TJ_LN_SWITCH(W)                                   \
+  if (!wide) {                                            \
+    switch (vpl) {                                        \
+      case 1: TJ_LN_CASE(1, 32, W); break;                \
+      case 2: TJ_LN_CASE(2, 32, W); break;                \
+      case 4: TJ_LN_CASE(4, 32, W); break;                \
+      case 8: TJ_LN_CASE(8, 32, W); break;                \
+      case 16: TJ_LN_CASE(16, 32, W); break;              \
+      default: TJ_LN_CASE(32, 32, W); break;              \
+    }                                                     \
+  } else {                                                \
+    switch (vpl) {                                        \
+      case 8: TJ_LN_CASE(8, kLnThreads, W); break;        \
+      case 16: TJ_LN_CASE(16, kLnThreads, W); break;      \
+      default: TJ_LN_CASE(32, kLnThreads, W); break;      \
+    }                                                     \
   }
+  if (VW == 4) {
+    TJ_LN_SWITCH(4)
+  } else {
+    TJ_LN_SWITCH(1)
+  }
+#undef TJ_LN_SWITCH
 #undef TJ_LN_CASE
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "ln_final_mask launch: %s", cudaGetErrorString(e));

@@ -119,7 +119,14 @@ class UserOptimizedTransformer(nn.Module):
     # ---- weight caches ------------------------------------------------------
     @staticmethod
     def _cast_cache(t: torch.Tensor) -> torch.Tensor:
-        return t.detach().to(dtype=torch.float16).contiguous()
+        """fp16 copy of an [N, K] weight with rows padded by zeros to a multiple
+        of 8 columns (whole 16-byte rows for the GEMM's TMA loads; the encoder
+        reads only the first K)."""
+        w = t.detach().to(dtype=torch.float16)
+        pad = -w.shape[1] % 8
+        if pad:
+            w = torch.nn.functional.pad(w, (0, pad))
+        return w.contiguous()
 
     def _refresh_mixed_weights(self) -> None:
         """Rebuilds the fp16 caches (v16_1_clean.py:412-442)."""

@@ -68,7 +68,9 @@ def test_token_plan(cuda_pkg, B, S):
 # D above 4096 runs a CTA per row (4100: 8 groups per thread, the last partly
 # used; 12288: 16; 32768: 32, the widest row).
 @pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (1000, 768), (513, 1024), (64, 4096),
-                                    (40, 4100), (33, 8192), (20, 12288), (9, 32768)])
+                                    (40, 4100), (33, 8192), (20, 12288), (9, 32768),
+                                    # D % 4 != 0: one column per group
+                                    (7, 30), (50, 1001), (3, 5001)])
 def test_ln_cast_and_final(cuda_pkg, rows, D):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(rows + D)
@@ -108,7 +110,7 @@ def test_ln_rejects_rows_above_32768(cuda_pkg):
 
 
 @pytest.mark.parametrize("rows,D", [(5, 16), (300, 256), (513, 1024), (64, 4096), (17, 8192),
-                                    (9, 32768)])
+                                    (9, 32768), (9, 30), (5, 5001)])
 def test_add_ln_cast_and_final(cuda_pkg, rows, D):
     """Residual add (fp32 x + fp16 branch output) fused into the LayerNorm."""
     k = cuda_pkg.kernels

@@ -185,12 +185,19 @@ def test_rejects_unsupported_inputs(cuda_pkg):
     model.train()
     with pytest.raises(RuntimeError):
         model(torch.zeros(1, 128, 256, device=DEV))
-    # fp16 GEMM operand rows must be whole 16-byte units: d_model 100 is refused
-    # before any kernel runs.
-    cfg = oracle.TransformerConfig(1, 16, 100, 4, 64, 1, False)
-    model = _model(cuda_pkg, cfg, oracle.make_state_dict(cfg, seed=1))
-    with pytest.raises(RuntimeError, match="multiples of 8"):
-        model(torch.zeros(1, 16, 100, device=DEV))
+
+
+@pytest.mark.parametrize("cfg_t,pad", [((2, 64, 100, 4, 200, 1, False), 0.3),   # D % 8 = 4, head dim 25
+                                       ((2, 48, 30, 3, 70, 2, True), 0.2),     # D % 4 = 2, F % 8 = 6, causal
+                                       ((3, 40, 36, 4, 36, 1, False), 0.5)])   # head dim 9, F % 8 = 4
+def test_widths_not_multiples_of_8(cuda_pkg, cfg_t, pad):
+    """d_model / ffn_dim that are not multiples of 8: fp16 rows padded to 8
+    columns, GEMMs reading the true K, scalar LayerNorm rows when D % 4 != 0."""
+    cfg = oracle.TransformerConfig(*cfg_t)
+    sd = oracle.make_state_dict(cfg, seed=29)
+    x, mask = oracle.generate_random_case(cfg, seed=29, padding_ratio=pad)
+    out = _run(_model(cuda_pkg, cfg, sd), x, mask)
+    _gate(oracle.encoder_forward(sd, cfg, x, mask), out, f"{cfg_t}")
 
 
 def test_cuda_graph_replay_matches_eager(cuda_pkg):
