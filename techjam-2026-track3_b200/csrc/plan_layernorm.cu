@@ -21,14 +21,23 @@
 namespace tj {
 
 // ---------------------------------------------------------------------------
-// Token plan: one CTA of 1024 threads = 32 warps.  Warp w owns a contiguous
-// segment of the B*S mask bytes and reads it 32 bytes at a time (coalesced),
-// 16 groups per batch with every load issued before the first is used; a
-// ballot gives the valid lanes, popc their rank.  Pass 1 counts each segment,
-// a scan of the 32 counts gives each warp its first compact row, and pass 2
-// re-reads the segment and writes orig/inv/cu coalesced.
+// Token plan: CTAs of 1024 threads = 32 warps, CTA k owning the mask bytes
+// [k*seg, (k+1)*seg) (seg >= kPlanMinSeg, so at most kPlanMaxCtas CTAs).  No
+// CTA waits for another: each first counts the valid tokens before its
+// segment itself (16-byte loads over the mask ahead of it; cheap next to the
+// writes), then warp w owns a 32-byte-aligned part of the segment and reads it
+// 32 bytes at a time (coalesced), 16 groups per batch with every load issued
+// before the first is used; a ballot gives the valid lanes, popc their rank.
+// Pass 1 counts each part, a scan of the 32 counts (after the CTA's prefix)
+// gives each warp its first compact row, and pass 2 re-reads the part and
+// writes orig/inv/cu coalesced.  The CTA holding a sample's first token
+// position also writes that sample's count (reading the sample's tail past
+// its segment if needed), the last CTA the total, and CTA 0 the longest-first
+// sample order, for which it counts every sample's tokens on its own.
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanMinSeg = 4096;
+constexpr int kPlanMaxCtas = 256;
 constexpr int kPlanOrderMaxB = 256;  // batches up to this size get a longest-first order
 constexpr int kPlanBatch = 16;  // 32-byte groups loaded per batch
 
@@ -47,20 +56,73 @@ __device__ __forceinline__ uint32_t plan_load_batch(const uint8_t* __restrict__ 
   return bits;
 }
 
+// Sum over the CTA (every thread gets it; all must call).
+__device__ __forceinline__ int plan_block_sum(int v, int* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // red may still be read by an earlier sum
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int s = 0;
+#pragma unroll
+  for (int w = 0; w < kPlanThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+// Nonzero bytes of a 32-bit word.
+__device__ __forceinline__ int plan_nz4(uint32_t w) { return __popc(__vcmpne4(w, 0u)) >> 3; }
+
+// Valid tokens among mask bytes [lo, hi), counted by the whole CTA.
+__device__ int plan_count(const uint8_t* __restrict__ mask, int lo, int hi, int* red) {
+  int c = 0;
+  if (hi > lo) {
+    if (mask == nullptr) {
+      c = threadIdx.x == 0 ? hi - lo : 0;
+    } else {
+      const uintptr_t p_lo = reinterpret_cast<uintptr_t>(mask + lo);
+      const int a16 = min(hi, lo + (int)(((p_lo + 15) & ~(uintptr_t)15) - p_lo));
+      const int n16 = (hi - a16) >> 4;
+      const int b16 = a16 + 16 * n16;
+      for (int i = lo + (int)threadIdx.x; i < a16; i += kPlanThreads) c += mask[i] != 0;
+      const uint4* v = reinterpret_cast<const uint4*>(mask + a16);
+      for (int i = threadIdx.x; i < n16; i += kPlanThreads) {
+        const uint4 w = __ldg(v + i);
+        c += plan_nz4(w.x) + plan_nz4(w.y) + plan_nz4(w.z) + plan_nz4(w.w);
+      }
+      for (int i = b16 + (int)threadIdx.x; i < hi; i += kPlanThreads) c += mask[i] != 0;
+    }
+  }
+  return plan_block_sum(c, red);
+}
+
+static int plan_segment(int64_t total) {
+  int64_t seg = (total + kPlanMaxCtas - 1) / kPlanMaxCtas;
+  if (seg < kPlanMinSeg) seg = kPlanMinSeg;
+  return (int)((seg + 1023) / 1024 * 1024);  // whole 32-byte groups for each of the 32 warps
+}
+
 __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t* __restrict__ mask,
-                                                                  int B, int S,
+                                                                  int B, int S, int seg,
                                                                   int32_t* __restrict__ plan) {
+  __shared__ int red[32];
+  __shared__ int warp_base[32];
+  __shared__ int cnt_s[kPlanOrderMaxB];
   pdl_wait();
   const int total = B * S;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int seg = ((total + 31) / 32 + 31) / 32 * 32;  // multiple of 32 elements
-  const int begin = min(total, warp * seg);
-  const int end = min(total, begin + seg);
+  const int cb = (int)blockIdx.x * seg;
+  const int ce = min(total, cb + seg);
+  const int wseg = seg / 32;  // a multiple of 32
+  const int begin = min(ce, cb + warp * wseg);
+  const int end = min(ce, begin + wseg);
 
   int32_t* cu = plan + 1;
   int32_t* cnt = plan + 2 + B;
   int32_t* orig = plan + 2 + 2 * B;
   int32_t* inv = orig + total;
+  int32_t* order = inv + total;
+
+  const int prefix = plan_count(mask, 0, cb, red);
 
   int count = 0;
   for (int g0 = begin; g0 < end; g0 += 32 * kPlanBatch) {
@@ -68,7 +130,6 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
 #pragma unroll
     for (int k = 0; k < kPlanBatch; ++k) count += __popc(__ballot_sync(0xffffffffu, (bits >> k) & 1u));
   }
-  __shared__ int warp_base[32];
   if (lane == 0) warp_base[warp] = count;
   __syncthreads();
   if (warp == 0) {
@@ -80,13 +141,11 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
       if (lane >= o) incl += v;
     }
     warp_base[lane] = incl - w;
-    if (lane == 31) {
-      plan[0] = incl;
-      cu[B] = incl;
-    }
+    red[lane] = incl;  // lane 31: the segment's count (red is free until the next sum)
   }
   __syncthreads();
-  int run = warp_base[warp];
+  const int seg_end_row = prefix + red[31];  // compact row of the first token after the segment
+  int run = prefix + warp_base[warp];
   int next_start = (begin + S - 1) / S * S;  // first sample start at or after `begin`
   for (int g0 = begin; g0 < end; g0 += 32 * kPlanBatch) {
     const uint32_t bits = plan_load_batch(mask, g0, end, lane);
@@ -116,30 +175,74 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
       run += __popc(bal);
     }
   }
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
+    plan[0] = seg_end_row;
+    cu[B] = seg_end_row;
+  }
   __syncthreads();
   __threadfence_block();
-  int32_t* order = inv + total;
-  __shared__ int cnt_s[kPlanOrderMaxB];
-  for (int b = threadIdx.x; b < B; b += kPlanThreads) {
-    const int c = ((volatile int32_t*)cu)[b + 1] - ((volatile int32_t*)cu)[b];
-    cnt[b] = c;
-    if (B <= kPlanOrderMaxB) cnt_s[b] = c;
+  // Counts of the samples starting in this segment: up to the next start
+  // inside it, or to the segment end plus the sample's tokens past it.
+  const int b_first = (cb + S - 1) / S;
+  const int b_end = min(B, (ce + S - 1) / S);  // samples b_first .. b_end-1 start here
+  if (b_first < b_end) {
+    const volatile int32_t* vcu = cu;
+    for (int bb = b_first + (int)threadIdx.x; bb < b_end; bb += kPlanThreads)
+      if ((bb + 1) * S <= ce) cnt[bb] = ((bb + 1) * S < ce ? vcu[bb + 1] : seg_end_row) - vcu[bb];
+    const int bl = b_end - 1;  // the last one may run past the segment
+    if ((bl + 1) * S > ce) {
+      const int tail = plan_count(mask, ce, (bl + 1) * S, red);
+      if (threadIdx.x == 0) cnt[bl] = seg_end_row - vcu[bl] + tail;
+    }
   }
   // Samples by decreasing valid-token count (stable): attention launches its
   // CTAs for the longest samples first, so the last wave holds short ones.
-  if (B <= kPlanOrderMaxB) {
-    __syncthreads();
-    for (int b = threadIdx.x; b < B; b += kPlanThreads) {
-      const int c = cnt_s[b];
-      int rank = 0;
-      for (int o = 0; o < B; ++o) {
-        const int co = cnt_s[o];
-        rank += (co > c || (co == c && o < b)) ? 1 : 0;
+  if (blockIdx.x == 0) {
+    if (B <= kPlanOrderMaxB) {
+      for (int bb = threadIdx.x; bb < B; bb += kPlanThreads) cnt_s[bb] = mask ? 0 : S;
+      __syncthreads();
+      if (mask) {
+        // Each thread counts a contiguous stretch of the mask, one
+        // shared-memory add per sample it touches: 16 bytes per load where
+        // the address is 16-byte aligned and the 16 bytes lie in one sample
+        // and the stretch, single bytes elsewhere (after a sample boundary
+        // until the next aligned address).
+        const uintptr_t base = reinterpret_cast<uintptr_t>(mask);
+        const int per = ((total + kPlanThreads - 1) / kPlanThreads + 15) & ~15;
+        const int lo = min(total, (int)threadIdx.x * per), hi = min(total, lo + per);
+        int cur = lo / S, acc = 0;
+        int64_t next_b = (int64_t)(cur + 1) * S;
+        for (int i = lo; i < hi;) {
+          if (((base + (uintptr_t)i) & 15u) == 0 && i + 16 <= hi && i + 16 <= next_b) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(mask + i));
+            acc += plan_nz4(w.x) + plan_nz4(w.y) + plan_nz4(w.z) + plan_nz4(w.w);
+            i += 16;
+          } else {
+            acc += mask[i] != 0;
+            ++i;
+          }
+          if (i == next_b) {
+            if (acc) atomicAdd(&cnt_s[cur], acc);
+            acc = 0;
+            ++cur;
+            next_b += S;
+          }
+        }
+        if (acc) atomicAdd(&cnt_s[cur], acc);
       }
-      order[rank] = b;
+      __syncthreads();
+      for (int bb = threadIdx.x; bb < B; bb += kPlanThreads) {
+        const int c = cnt_s[bb];
+        int rank = 0;
+        for (int o = 0; o < B; ++o) {
+          const int co = cnt_s[o];
+          rank += (co > c || (co == c && o < bb)) ? 1 : 0;
+        }
+        order[rank] = bb;
+      }
+    } else {
+      for (int bb = threadIdx.x; bb < B; bb += kPlanThreads) order[bb] = bb;
     }
-  } else {
-    for (int b = threadIdx.x; b < B; b += kPlanThreads) order[b] = b;
   }
   pdl_trigger();
 }
@@ -151,7 +254,9 @@ int launch_token_plan(const uint8_t* mask, int B, int S, int32_t* plan, cudaStre
   if ((int64_t)B * S > (int64_t)INT32_MAX - 1)
     return set_error(TJ_ERR_UNSUPPORTED, "token_plan: B*S=%lld exceeds int32", (long long)B * S);
   if (plan == nullptr) return set_error(TJ_ERR_INVALID_ARGUMENT, "token_plan: null plan buffer");
-  cudaError_t e = launch_pdl(token_plan_kernel, dim3(1), dim3(kPlanThreads), 0, stream, mask, B, S, plan);
+  const int seg = plan_segment((int64_t)B * S);
+  const int ctas = (int)(((int64_t)B * S + seg - 1) / seg);
+  cudaError_t e = launch_pdl(token_plan_kernel, dim3(ctas), dim3(kPlanThreads), 0, stream, mask, B, S, seg, plan);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "token_plan launch: %s", cudaGetErrorString(e));
   return TJ_OK;
@@ -265,17 +370,30 @@ __global__ void __launch_bounds__(kLnThreads) ln_cast_f16_kernel(
   if (row >= limit) return;  // uniform for the RT threads of a row
   const int64_t src = row_map ? (int64_t)row_map[row] : (int64_t)row;
   const float* xr = x + src * D;
+  // Every load of the row is issued before the first use.
   float v[VPL][VW];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int g = i * RT + k;
     if (g * VW < D) {
       ln_load<VW>(xr, g, v[i]);
-      if (add16) ln_add_f16<VW>(add16 + (int64_t)row * ld_add, g, v[i]);
-      if (sum_out) ln_store<VW>(sum_out + (int64_t)row * D, g, v[i]);
     } else {
 #pragma unroll
       for (int e = 0; e < VW; ++e) v[i][e] = 0.f;
+    }
+  }
+  if (add16) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int g = i * RT + k;
+      if (g * VW < D) ln_add_f16<VW>(add16 + (int64_t)row * ld_add, g, v[i]);
+    }
+  }
+  if (sum_out) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int g = i * RT + k;
+      if (g * VW < D) ln_store<VW>(sum_out + (int64_t)row * D, g, v[i]);
     }
   }
   float mean, rstd;
@@ -330,17 +448,30 @@ __global__ void __launch_bounds__(kLnThreads) ln_final_kernel(const float* __res
     return;
   }
   const float* xr = x + (x_at_original ? (int64_t)row : src) * D;
+  // Every load of the row is issued before the first use.
   float v[VPL][VW];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int g = i * RT + k;
     if (g * VW < D) {
       ln_load<VW>(xr, g, v[i]);
-      if (add16) ln_add_f16<VW>(add16 + src * ld_add, g, v[i]);
-      if (add16b) ln_add_f16<VW>(add16b + src * ld_add, g, v[i]);
     } else {
 #pragma unroll
       for (int e = 0; e < VW; ++e) v[i][e] = 0.f;
+    }
+  }
+  if (add16) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int g = i * RT + k;
+      if (g * VW < D) ln_add_f16<VW>(add16 + src * ld_add, g, v[i]);
+    }
+  }
+  if (add16b) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int g = i * RT + k;
+      if (g * VW < D) ln_add_f16<VW>(add16b + src * ld_add, g, v[i]);
     }
   }
   float mean, rstd;

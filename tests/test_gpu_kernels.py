@@ -35,8 +35,15 @@ def _plan_reference(mask):
     return orig, inv, counts, cu
 
 
-@pytest.mark.parametrize("B,S", [(1, 1), (2, 8), (40, 7), (33, 33), (3, 1000), (8, 2048), (1, 131072)])
-def test_token_plan(cuda_pkg, B, S):
+# The plan runs one CTA per >= 4096 mask bytes (at most 256 CTAs): samples
+# cross CTA segments (5x3001, 1x131072), many start inside one (20000x1,
+# 300x129: above 256 samples the order is the identity), 3x1000003 spreads
+# over 256 CTAs, and a mask that starts off a 16-byte boundary takes the
+# byte-load path.
+@pytest.mark.parametrize("B,S,offset", [(1, 1, 0), (2, 8, 0), (40, 7, 0), (33, 33, 0), (3, 1000, 0),
+                                        (8, 2048, 0), (1, 131072, 0), (5, 3001, 0), (20000, 1, 0),
+                                        (300, 129, 0), (3, 1000003, 0), (8, 2048, 1), (5, 3001, 3)])
+def test_token_plan(cuda_pkg, B, S, offset):
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(B * 7 + S)
     lengths = torch.randint(0, S + 1, (B,), generator=g)
@@ -44,7 +51,10 @@ def test_token_plan(cuda_pkg, B, S):
     if B >= 3:
         mask[1] = torch.rand(S, generator=g) < 0.3  # a non-prefix row
         mask[0] = False  # an all-padded row
-    plan = k.token_plan(mask.to(DEV), B, S, DEV)
+    store = torch.zeros(B * S + offset, dtype=torch.bool, device=DEV)
+    dmask = store[offset:].view(B, S)
+    dmask.copy_(mask.to(DEV))
+    plan = k.token_plan(dmask, B, S, DEV)
     nv, cu, cnt, orig, inv = [t.cpu() for t in k.plan_views(plan, B, S)]
     r_orig, r_inv, r_cnt, r_cu = _plan_reference(mask)
     assert int(nv) == int(mask.sum())
@@ -63,6 +73,8 @@ def test_token_plan(cuda_pkg, B, S):
     nv, cu, cnt, orig, inv = [t.cpu() for t in k.plan_views(plan, B, S)]
     assert int(nv) == B * S
     assert torch.equal(orig, torch.arange(B * S, dtype=torch.int32))
+    assert torch.equal(cnt, torch.full((B,), S, dtype=torch.int32))
+    assert torch.equal(cu, torch.arange(B + 1, dtype=torch.int32) * S)
 
 
 # D above 4096 runs a CTA per row (4100: 8 groups per thread, the last partly
