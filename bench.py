@@ -12,8 +12,11 @@ non-causal, right-padded mask with lengths ~ U[1024, 2048], LayerNorm
 gamma ~ 1+0.02N(0,1), beta ~ 0.02N(0,1), seeded default-init weights.
 
 Multi-GPU (torchrun, one rank per GPU): batch sharding with no data-path
-collective; each rank runs its own B=8 batch (weak scaling).  The step time is
-the max over ranks of the CUDA-event time of the K timed steps.
+collective.  `dense` (and `short`): each rank runs its own batch (weak
+scaling).  `batch`: one global batch of 32 sequences split evenly over the
+ranks (strong scaling), the output all-gather timed separately.  `long`: one
+sequence sharded over the ranks (context parallel).  The step time is the
+max over ranks of the CUDA-event time of the K timed steps.
 
 Rank 0 prints one JSON line.  `--impl reference` times the reference's CPU
 FP32 path (the oracle restatement of BaselineTransformer) on the host cores.
@@ -172,7 +175,14 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # Workload construction
 # ---------------------------------------------------------------------------
-def build_case(workload, rank, device):
+# Workloads whose global batch is split over the ranks (strong scaling).
+SPLIT_BATCH = ("batch",)
+
+
+def build_case(workload, rank, device, world=1):
+    """Config, weights and this rank's input.  Split-batch workloads draw one
+    global batch and return rank `rank`'s contiguous 1/world of it; the others
+    draw a batch per rank."""
     import oracle
 
     B, S, D, H, F, L, causal, pad, ln, _ = WORKLOADS[workload]
@@ -181,7 +191,15 @@ def build_case(workload, rank, device):
     if ln:
         sd = oracle.perturb_layernorm(sd, 1234)
     # Timing inputs use seed + 100000 as the reference harness does
-    # (torch_transformer_benchmark.py:533); each rank draws its own batch.
+    # (torch_transformer_benchmark.py:533).
+    if workload in SPLIT_BATCH:
+        if B % world != 0:
+            raise SystemExit(f"--workload {workload}: batch {B} does not split over {world} GPUs")
+        x, mask = oracle.generate_random_case(cfg, seed=1234 + 100000, padding_ratio=pad)
+        n = B // world
+        x, mask = x[rank * n:(rank + 1) * n].contiguous(), mask[rank * n:(rank + 1) * n].contiguous()
+        cfg = oracle.TransformerConfig(n, S, D, H, F, L, causal)
+        return cfg, sd, x, mask
     x, mask = oracle.generate_random_case(cfg, seed=1234 + 100000 + 7919 * rank, padding_ratio=pad)
     return cfg, sd, x, mask
 
@@ -289,7 +307,8 @@ def run_ours(args, world, rank, local):
     torch.cuda.set_device(device)
     init_dist(world, "nccl")
     pkg = __graft_entry__.load_package()
-    cfg, sd, x_cpu, mask_cpu = build_case(args.workload, rank, device)
+    split = args.workload in SPLIT_BATCH
+    cfg, sd, x_cpu, mask_cpu = build_case(args.workload, rank, device, world)
     B, S, D = cfg.batch_size, cfg.seq_len, cfg.d_model
     model = pkg.UserOptimizedTransformer(pkg.TransformerConfig(*cfg.__dict__.values()))
     model.load_state_dict(sd, strict=True)
@@ -329,6 +348,7 @@ def run_ours(args, world, rank, local):
     tokens_per_step = B * S * world
     value = tokens_per_step / (ms_step / 1e3)
 
+    gather = measure_output_gather(model, xs[0], mask, device, world) if split and world > 1 else None
     e2e = {"unavailable": "input larger than 2 GiB"} if big else measure_e2e(model, x_cpu, mask_cpu, device, args, world)
     kernels = None if big else kernel_breakdown(pkg, model, cfg, xs[0], mask, device, args)
     nv, gemm_flops, attn_flops = algorithmic_work(cfg, mask_cpu)
@@ -351,7 +371,7 @@ def run_ours(args, world, rank, local):
             "warmup": args.warmup,
             "ms_per_step": ms_step,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if split else "weak",
             "vs_baseline": None,
             "dtype": "fp16 operands, fp32 accumulate/LayerNorm/residual/output",
             "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
@@ -363,7 +383,9 @@ def run_ours(args, world, rank, local):
                 "heads": cfg.num_heads,
                 "ffn_dim": cfg.ffn_dim,
                 "layers": cfg.num_layers,
-                "parallelism": f"batch-sharded x{world} (no data-path collective)",
+                "parallelism": (f"batch-sharded x{world}: the global batch split evenly, output all-gather "
+                                "timed apart (output_gather)" if split and world > 1
+                                else f"batch-sharded x{world} (no data-path collective)"),
                 "valid_tokens_per_gpu": int(nv),
                 "l2": f"inputs larger than L2: x rotates over {n_rot} buffers of {x_bytes / 2**20:.0f} MiB; "
                       "each step writes ~1 GB of activations",
@@ -376,12 +398,40 @@ def run_ours(args, world, rank, local):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if gather is not None:
+            gather["value_with_gather"] = tokens_per_step / ((ms_step + gather["ms"]) / 1e3)
+            line["output_gather"] = gather
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier(device_ids=[device.index])
         dist.destroy_process_group()
     return line
+
+
+def measure_output_gather(model, x, mask, device, world):
+    """The split batch's only collective: all-gather of every rank's fp32
+    output [B/world, S, D] into the full [B, S, D] on every rank (NCCL over
+    NVLink), timed on the device (max over ranks) over a few repeats."""
+    import torch.distributed as dist
+
+    with torch.inference_mode():
+        out = model(x, mask)
+        full = torch.empty((world * out.shape[0],) + tuple(out.shape[1:]), dtype=out.dtype, device=device)
+        for _ in range(2):
+            dist.all_gather_into_tensor(full, out)
+        torch.cuda.synchronize(device)
+        barrier(world, device)
+        reps = 5
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(reps):
+            dist.all_gather_into_tensor(full, out)
+        end.record()
+        torch.cuda.synchronize(device)
+    ms = max_over_ranks(world, start.elapsed_time(end) / reps, device)
+    return {"ms": ms, "bytes_per_rank": out.numel() * out.element_size(),
+            "collective": "all_gather_into_tensor (NCCL)"}
 
 
 def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
