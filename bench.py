@@ -196,9 +196,14 @@ def build_case(workload, rank, device, world=1):
         if B % world != 0:
             raise SystemExit(f"--workload {workload}: batch {B} does not split over {world} GPUs")
         x, mask = oracle.generate_random_case(cfg, seed=1234 + 100000, padding_ratio=pad)
-        n = B // world
-        x, mask = x[rank * n:(rank + 1) * n].contiguous(), mask[rank * n:(rank + 1) * n].contiguous()
-        cfg = oracle.TransformerConfig(n, S, D, H, F, L, causal)
+        if world > 1:
+            # B/world samples per rank, balanced by work (sharding.balanced_assignment).
+            from techjam_b200 import sharding
+
+            lengths = mask.to(torch.int64).sum(1).tolist()
+            mine = torch.tensor(sharding.balanced_assignment(lengths, world, D, F)[rank], dtype=torch.int64)
+            x, mask = x[mine].contiguous(), mask[mine].contiguous()
+            cfg = oracle.TransformerConfig(B // world, S, D, H, F, L, causal)
         return cfg, sd, x, mask
     x, mask = oracle.generate_random_case(cfg, seed=1234 + 100000 + 7919 * rank, padding_ratio=pad)
     return cfg, sd, x, mask
@@ -383,8 +388,9 @@ def run_ours(args, world, rank, local):
                 "heads": cfg.num_heads,
                 "ffn_dim": cfg.ffn_dim,
                 "layers": cfg.num_layers,
-                "parallelism": (f"batch-sharded x{world}: the global batch split evenly, output all-gather "
-                                "timed apart (output_gather)" if split and world > 1
+                "parallelism": (f"batch-sharded x{world}: the global batch split evenly (equal sample counts, "
+                                "balanced by work), output all-gather timed apart (output_gather)"
+                                if split and world > 1
                                 else f"batch-sharded x{world} (no data-path collective)"),
                 "valid_tokens_per_gpu": int(nv),
                 "l2": f"inputs larger than L2: x rotates over {n_rot} buffers of {x_bytes / 2**20:.0f} MiB; "

@@ -5,9 +5,10 @@ One process per GPU (torchrun), torch.distributed for the plumbing.
 * Batch sharding: samples are independent in the reference model (every op
   is per sample), so each rank runs a contiguous, balanced range of the batch
   (the balanced-range split of the reference's multi-stream variant,
-  candidates/v19/parallel_batch_common.py:31-51) with no data-path
-  collective; `BatchShardedEncoder.forward(..., gather=True)` optionally
-  all-gathers the outputs.
+  candidates/v19/parallel_batch_common.py:31-51) or, balanced by estimated
+  work rather than count, the sample set of `balanced_assignment`, with no
+  data-path collective; `BatchShardedEncoder.forward(..., gather=True)`
+  optionally all-gathers the outputs (back in batch order).
 * Context parallelism for one long sequence: rank g holds a contiguous chunk
   of the sequence.  Attention is the only op that mixes tokens, so each rank
   computes LN1 and the QKV projection for its own tokens, all-gathers the
@@ -63,8 +64,34 @@ def sequence_ranges(valid: torch.Tensor, world: int) -> List[Tuple[int, int]]:
     return [(bounds[r], bounds[r + 1]) for r in range(world)]
 
 
+def balanced_assignment(lengths: Sequence[int], world: int, d_model: int, ffn_dim: int) -> List[List[int]]:
+    """Samples per rank, balanced by estimated work instead of sample count.
+
+    Each rank gets as many samples as `batch_ranges` gives it (equal shapes
+    everywhere), chosen greedily, largest first, for the rank with the least
+    work so far (ties to the lower rank, so every rank computes the same
+    assignment).  A sample of L valid tokens costs L (projections, per
+    token) + w * L^2 (attention), w = attention FLOPs per token pair over
+    projection FLOPs per token, doubled because attention runs at about half
+    the projections' tensor-core rate.  Returns sorted index lists."""
+    B = len(lengths)
+    caps = [e - s for s, e in batch_ranges(B, world)]
+    w = 2.0 * (4.0 * d_model) / (8.0 * d_model * d_model + 4.0 * d_model * ffn_dim)
+    cost = [float(L) + w * float(L) * float(L) for L in lengths]
+    out: List[List[int]] = [[] for _ in range(world)]
+    load = [0.0] * world
+    for i in sorted(range(B), key=lambda i: (-cost[i], i)):
+        r = min((r for r in range(world) if len(out[r]) < caps[r]), key=lambda r: (load[r], r))
+        out[r].append(i)
+        load[r] += cost[i]
+    return [sorted(o) for o in out]
+
+
 class BatchShardedEncoder:
-    """Runs `model` on this rank's range of the batch."""
+    """Runs `model` on this rank's share of the batch: a contiguous range
+    (`local_range`), or the work-balanced sample set of `balanced_assignment`
+    (`local_samples`), in which case `forward(..., gather=True, assignment=a)`
+    puts the gathered outputs back in batch order."""
 
     def __init__(self, model, group=None) -> None:
         import torch.distributed as dist
@@ -77,7 +104,14 @@ class BatchShardedEncoder:
     def local_range(self, batch: int) -> Tuple[int, int]:
         return batch_ranges(batch, self.world)[self.rank]
 
-    def forward(self, x_local: torch.Tensor, mask_local: Optional[torch.Tensor], gather: bool = False):
+    def assignment(self, valid_token_mask: torch.Tensor) -> List[List[int]]:
+        """The work-balanced split of a [B, S] mask (the same on every rank)."""
+        cfg = self.model.config
+        lengths = valid_token_mask.to(torch.int64).sum(1).tolist()
+        return balanced_assignment(lengths, self.world, cfg.d_model, cfg.ffn_dim)
+
+    def forward(self, x_local: torch.Tensor, mask_local: Optional[torch.Tensor], gather: bool = False,
+                assignment: Optional[Sequence[Sequence[int]]] = None):
         # A rank may hold no samples (batch < world); it still joins the gather.
         out = self.model(x_local, mask_local)
         if not gather or self.world == 1:
@@ -89,7 +123,15 @@ class BatchShardedEncoder:
         sizes = [int(s.item()) for s in sizes]
         parts = [torch.empty((n,) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device) for n in sizes]
         dist.all_gather(parts, out.contiguous(), group=self.group)
-        return torch.cat(parts, 0)
+        full = torch.cat(parts, 0)
+        if assignment is None:
+            return full
+        order = torch.tensor([i for r in assignment for i in r], dtype=torch.int64, device=full.device)
+        if order.numel() != full.shape[0]:
+            raise ValueError("assignment does not cover the gathered batch")
+        result = torch.empty_like(full)
+        result[order] = full
+        return result
 
 
 def segment_metadata(counts: torch.Tensor, rank: int, causal: bool):

@@ -56,6 +56,12 @@ def main() -> int:
         full = model(x.to(dev), mask.to(dev))
         if not torch.equal(out, full):
             failures.append(f"batch sharding differs from one GPU: {float((out - full).abs().max())}")
+        # work-balanced sample sets, gathered back into batch order
+        assign = bs.assignment(mask)
+        mine = torch.tensor(assign[rank], dtype=torch.int64)
+        out = bs.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign)
+        if not torch.equal(out, full):
+            failures.append(f"balanced batch sharding differs from one GPU: {float((out - full).abs().max())}")
 
         # ---- context parallelism -------------------------------------------
         for cfg_t, pad in (((1, 4096, 1024, 16, 4096, 1, False), 0.1), ((1, 3000, 512, 8, 1024, 2, True), 0.2)):

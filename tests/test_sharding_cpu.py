@@ -32,6 +32,26 @@ def test_batch_ranges(pkg):
             assert max(sizes) - min(sizes) <= 1
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_balanced_assignment(pkg, world):
+    """Every sample exactly once, the per-rank counts of batch_ranges, and the
+    most loaded rank no worse than with contiguous ranges."""
+    from techjam_b200 import sharding
+
+    g = torch.Generator().manual_seed(world)
+    for B in (0, 1, 7, 32, 33):
+        lengths = torch.randint(1, 4097, (B,), generator=g).tolist()
+        a = sharding.balanced_assignment(lengths, world, 1024, 4096)
+        assert sorted(i for r in a for i in r) == list(range(B))
+        assert [len(r) for r in a] == [e - s for s, e in sharding.batch_ranges(B, world)]
+        assert a == sharding.balanced_assignment(lengths, world, 1024, 4096)  # deterministic
+        w = 2.0 * 4096 / (8 * 1024 * 1024 + 4 * 1024 * 4096)
+        cost = [L + w * L * L for L in lengths]
+        worst = max((sum(cost[i] for i in r) for r in a), default=0.0)
+        worst_ranges = max((sum(cost[s:e]) for s, e in sharding.batch_ranges(B, world)), default=0.0)
+        assert worst <= worst_ranges + 1e-6
+
+
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_sequence_ranges_balance_valid_tokens(pkg, world):
     from techjam_b200 import sharding
