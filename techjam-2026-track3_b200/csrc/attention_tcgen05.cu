@@ -1,7 +1,9 @@
-// Masked flash attention forward on tcgen05 (head_dim 64), replacing the SDPA
-// call of v16_1_clean.py:505-514 (non-causal, [B,1,1,S] key mask) and :491-504
+// Masked flash attention forward on tcgen05, replacing the SDPA call of
+// v16_1_clean.py:505-514 (non-causal, [B,1,1,S] key mask) and :491-504
 // (causal), i.e. softmax(QK^T*scale)V of the FP32 reference,
 // torch_transformer_benchmark.py:97-117, with the score matrix never stored.
+// Heads are zero-padded to P = 64, 128 or 256 columns (AttnCfg below); the
+// description here is the P = 64 instance, the one the dense layers run.
 //
 // Queries and keys are compact: the token plan packs the valid tokens of each
 // sample densely, so a sample's keys are the rows [off, off+len) of its key
@@ -19,15 +21,16 @@
 //                   O_t += P_t V_j     (TS: P from TMEM, V from shared, 8 x K=16)
 //   warps 4-7     softmax for query tile 0, warps 8-11 for query tile 1;
 //                 thread = query row = TMEM lane.
-// TMEM (512 columns): tile t uses S [256t, +128), P [256t+128, +64) (fp16
-// pairs), O [256t+192, +64) (fp32).
+// TMEM (512 columns): tile t uses O [256t, +64) (fp32), S [256t+64, +128) and
+// P [256t+192, +64) (fp16 pairs).
 //
 // Softmax per key tile: load the S row, mask only on partial/causal tiles,
 // tree max; the running max is only raised when the new max exceeds it by
 // more than 8 (log2 units), in which case O (in TMEM) and the row sum are
 // rescaled -- otherwise P = exp2(s*scale*log2e - m) stays <= 2^8, safe in fp16.
 // P goes back to TMEM as fp16 and the tensor core accumulates O += P V; the
-// two query tiles' softmax warpgroups alternate with the tensor core.
+// two query tiles' softmax warpgroups take turns on the exponentials while the
+// tensor core works for the other tile.
 #include "common.cuh"
 #include "internal.h"
 

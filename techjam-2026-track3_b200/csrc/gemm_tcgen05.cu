@@ -1,9 +1,10 @@
 // Persistent tcgen05 GEMM, C[M,N] = A[M,K] * W[N,K]^T with fp16 operands and an
-// fp32 TMEM accumulator, and the three epilogues the encoder layer needs:
+// fp32 TMEM accumulator, and the epilogues of the encoder layer's projections:
 //
 //   kEpiQkvHeadMajor  QKV projection (v16_1_clean.py:474-489): +bias, fp16,
-//                     stored straight into the head-major [3][H][rows][dh]
-//                     layout attention reads, so no permute/contiguous pass.
+//                     stored straight into the head-major [3][H][rows][P]
+//                     layout attention reads (heads zero-padded to P = 64, 128
+//                     or 256 columns), so no permute/contiguous pass.
 //   kEpiResidualF32   output projection (v16_1_clean.py:516-523 + :620) and
 //                     FFN-out (v16_1_clean.py:533-537 + :621): +bias, +fp32
 //                     residual, fp32 store.
@@ -25,7 +26,11 @@
 // Two accumulators let the epilogue of tile i overlap the main loop of tile
 // i+1.  Tiles are walked n-fastest so CTAs running at the same time share the
 // A tile through L2.  The number of rows comes from device memory (the token
-// plan), so the host never synchronises to learn it.
+// plan), so the host never synchronises to learn it.  Large problems run the
+// CTA-pair variant (gemm_tcgen05_pair_kernel: two SMs per 256x256 tile with
+// tcgen05.mma.cta_group::2, each loading half of A and half of W).  Row
+// strides may exceed K (rows padded to whole 16-byte units); the tile loads
+// stop at K and zero-fill the rest of the last k-block.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
