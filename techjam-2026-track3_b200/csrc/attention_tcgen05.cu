@@ -80,7 +80,7 @@ struct AttnCfg {
   static_assert(NT == 1 || kPCol + BN / 2 <= kTileStride, "two query tiles must fit in TMEM");
   static_assert(kPCol + BN / 2 <= kTmemCols, "query tile must fit in TMEM");
   static_assert(kSmem * kMinBlocks <= 232448, "shared memory");
-  static_assert(STAGES <= 4, "barrier slots");
+  static_assert(STAGES <= 8, "barrier slots");
 };
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 256 between rescales
 // Of every 8 exponential pairs, this many run as a polynomial on the FMA pipe
@@ -192,25 +192,27 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
   uint8_t* sK = sQ + NT * kQBytes;          // kKVStages x CH chunks of BN rows
   uint8_t* sV = sK + kKVStages * kKVBytes;  // kKVStages x CH chunks of BN rows
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKVStages * kKVBytes);
-  // q_full, k_full[4], v_full[4], k_empty[4], v_empty[4], vfix[4],
-  // s_full[2], s_empty[2], p_full[2], pv_done[2], final, exp_done0[4], exp_done1[4]
+  // Barriers (8-byte slots, room for 8 K/V stages): q_full, k_full[8],
+  // v_full[8], k_empty[8], v_empty[8], vfix[8], s_full[2], s_empty[2],
+  // p_full[2], pv_done[2], final, exp_done0[4], exp_done1[4]; then the TMEM
+  // base address and the abort flag.
   const uint32_t q_full = smem_u32(bars + 0);
   auto k_full = [&](int s) { return smem_u32(bars + 1 + s); };
-  auto v_full = [&](int s) { return smem_u32(bars + 5 + s); };
-  auto k_empty = [&](int s) { return smem_u32(bars + 9 + s); };
-  auto v_empty = [&](int s) { return smem_u32(bars + 13 + s); };
+  auto v_full = [&](int s) { return smem_u32(bars + 9 + s); };
+  auto k_empty = [&](int s) { return smem_u32(bars + 17 + s); };
+  auto v_empty = [&](int s) { return smem_u32(bars + 25 + s); };
   // vfix[s]: the producer has zeroed the V rows past the segment end of the
   // partial tile in stage s (one phase per partial tile that used the stage).
-  auto vfix = [&](int s) { return smem_u32(bars + 17 + s); };
-  auto s_full = [&](int t) { return smem_u32(bars + 21 + t); };
-  auto s_empty = [&](int t) { return smem_u32(bars + 23 + t); };
-  auto p_full = [&](int t) { return smem_u32(bars + 25 + t); };
-  auto pv_done = [&](int t) { return smem_u32(bars + 27 + t); };
-  const uint32_t final_bar = smem_u32(bars + 29);
+  auto vfix = [&](int s) { return smem_u32(bars + 33 + s); };
+  auto s_full = [&](int t) { return smem_u32(bars + 41 + t); };
+  auto s_empty = [&](int t) { return smem_u32(bars + 43 + t); };
+  auto p_full = [&](int t) { return smem_u32(bars + 45 + t); };
+  auto pv_done = [&](int t) { return smem_u32(bars + 47 + t); };
+  const uint32_t final_bar = smem_u32(bars + 49);
   // exp_done{t}[q]: the softmax warp of query tile t on SM sub-partition q has
   // issued the exponentials of its current key tile (see the softmax loop).
-  auto exp_done = [&](int t, int q) { return smem_u32(bars + 30 + 4 * t + q); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 38);
+  auto exp_done = [&](int t, int q) { return smem_u32(bars + 50 + 4 * t + q); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 58);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_idx();
