@@ -48,6 +48,15 @@ def test_argument_errors_are_reported_without_gpu(pkg):
     assert need >= rows * (1024 * 2 * 4 + 1024 * 4 * 2 + 4096 * 2)
     bad = pkg._lib.EncoderDesc(8, 2048, 1000, 16, 4096, 1, 0, 1e-5)  # D % H != 0
     assert lib.tj_encoder_workspace_bytes(ctypes.byref(bad)) == 0
+    # Widths that are not multiples of 8: fp16 rows padded to 8 columns, so
+    # the workspace is that of the padded widths (same plan and fp32 rows).
+    odd = pkg._lib.EncoderDesc(2, 64, 100, 4, 200, 1, 0, 1e-5)
+    pad = pkg._lib.EncoderDesc(2, 64, 104, 4, 200, 1, 0, 1e-5)
+    n_odd = lib.tj_encoder_workspace_bytes(ctypes.byref(odd))
+    n_pad = lib.tj_encoder_workspace_bytes(ctypes.byref(pad))
+    assert 0 < n_odd <= n_pad
+    rows = 2 * 64
+    assert n_pad - n_odd <= 2 * rows * 4 * 4 + 4 * 256  # only the two fp32 row buffers differ (+ alignment)
     # Without a CUDA device every compute entry point refuses with a status code.
     rc = lib.tj_token_plan(None, 2, 8, None, None)
     assert rc != 0
