@@ -710,6 +710,52 @@ def run_reference(args, world, rank):
     }
 
 
+def attention_length_scan(args):
+    """Attention alone (head dim 64, 16 heads, non-causal, every sample of
+    length L, B*L fixed where possible) over L = 256 .. 65536: throughput per
+    length and the time per CTA and per 128-key step, which separates the
+    per-CTA fixed cost (set-up, pipeline fill, output) from the steady state.
+    Synthetic N(0,1) Q/K/V resident in HBM; CUDA events on the launching
+    stream; one JSON line per length."""
+    import __graft_entry__
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    pkg = __graft_entry__.load_package()
+    k = pkg.kernels
+    peaks, _ = load_peaks()
+    H, dh = 16, 64
+    g = torch.Generator(device=device).manual_seed(1234)
+    for B, L in ((64, 256), (32, 512), (16, 1024), (8, 2048), (4, 4096), (2, 8192), (1, 16384), (1, 65536)):
+        rows = B * L
+        cu = torch.arange(B + 1, dtype=torch.int32, device=device) * L
+        cnt = torch.full((B, 1), L, dtype=torch.int32, device=device)
+        qkv = torch.randn(3, H, rows, dh, device=device, generator=g).half()
+        ctx = torch.empty(rows, H * dh, dtype=torch.float16, device=device)
+        fn = lambda: k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, cu[:-1].contiguous().view(-1, 1), cnt, L,
+                                      dh ** -0.5, out=ctx)
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        n = max(3, min(args.steps, 20 if L < 65536 else 3))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize(device)
+        us = s.elapsed_time(e) * 1e3 / n
+        flops = 4.0 * B * H * L * L * dh
+        ctas = B * H * ((L + 255) // 256)  # two 128-query tiles per CTA
+        steps = (L + 127) // 128            # 128-key steps per CTA
+        print(json.dumps({"attention_scan": {"B": B, "L": L, "H": H, "head_dim": dh, "us": us,
+                                              "tflops": flops / us / 1e6,
+                                              "of_measured_peak": flops / us / 1e6 / peaks["bf16_tflops"],
+                                              "ctas": ctas, "steps_per_cta": steps,
+                                              "us_per_cta_step_per_sm": us * 148 / (ctas * steps)}}),
+              flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -719,12 +765,17 @@ def main():
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="dense")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attention-scan", action="store_true",
+                    help="time the attention kernel alone over sequence lengths 256..65536 instead")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     world, rank, local = dist_env()
     if world != args.gpus and world > 1:
         ap.error(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.attention_scan:
+        attention_length_scan(args)
+        return
     if args.impl == "reference":
         line = run_reference(args, world, rank)
     else:
