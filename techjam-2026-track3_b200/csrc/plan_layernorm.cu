@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
   int32_t* inv = orig + total;
   int32_t* order = inv + total;
 
-  const int prefix = plan_count(mask, 0, cb, red);
+  const int prefix = cb > 0 ? plan_count(mask, 0, cb, red) : 0;  // uniform for the CTA
 
   int count = 0;
   for (int g0 = begin; g0 < end; g0 += 32 * kPlanBatch) {
@@ -198,7 +198,12 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
   // Samples by decreasing valid-token count (stable): attention launches its
   // CTAs for the longest samples first, so the last wave holds short ones.
   if (blockIdx.x == 0) {
-    if (B <= kPlanOrderMaxB) {
+    if (B <= kPlanOrderMaxB && gridDim.x == 1) {
+      // One CTA holds the whole mask: this CTA wrote every count above.
+      __syncthreads();
+      __threadfence_block();
+      for (int bb = threadIdx.x; bb < B; bb += kPlanThreads) cnt_s[bb] = ((volatile int32_t*)cnt)[bb];
+    } else if (B <= kPlanOrderMaxB) {
       for (int bb = threadIdx.x; bb < B; bb += kPlanThreads) cnt_s[bb] = mask ? 0 : S;
       __syncthreads();
       if (mask) {
@@ -230,6 +235,8 @@ __global__ void __launch_bounds__(kPlanThreads) token_plan_kernel(const uint8_t*
         }
         if (acc) atomicAdd(&cnt_s[cur], acc);
       }
+    }
+    if (B <= kPlanOrderMaxB) {
       __syncthreads();
       for (int bb = threadIdx.x; bb < B; bb += kPlanThreads) {
         const int c = cnt_s[bb];
