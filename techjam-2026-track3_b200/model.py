@@ -11,9 +11,11 @@ rebuilt on load_state_dict/_apply (v16_1_clean.py:412-464).
 forward(x [B,S,D] fp32 CUDA, valid_token_mask [B,S] bool or None) runs the
 whole encoder as one tj_encoder_forward call on the current stream: token
 plan, then per layer LN1->fp16, QKV GEMM (head-major), flash attention,
-out-proj+residual, LN2->fp16, FFN-in+GELU, FFN-out+residual, then final
-LayerNorm with padded rows zeroed.  There is no eager or CPU fallback: a CPU
-tensor, a non-fp32 input, training mode or a missing library raises.
+out-proj (fp16), residual add + LN2->fp16, FFN-in+GELU, FFN-out (fp16), and
+the residual add fused into the next layer's LN1 or the final LayerNorm,
+which scatters back to [B,S,D] with padded rows zeroed.  There is no eager or
+CPU fallback: a CPU tensor, a non-fp32 input, training mode or a missing
+library raises.
 """
 from __future__ import annotations
 
