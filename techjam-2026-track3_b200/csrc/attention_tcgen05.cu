@@ -103,6 +103,7 @@ struct AttnKernelParams {
   int ld_ctx;
   int dh_out;  // real head dim (<= DH): columns of ctx written per head
   const int32_t* order;  // optional: sample handled by grid row z (longest first)
+  int z0;                // first grid row of this launch (batches above 65535 take several)
 };
 
 // Walks the key tiles of one sample in order: segment g, tile i inside it.
@@ -173,7 +174,8 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
   constexpr uint32_t kQBytes = Cfg::kQBytes, kKVBytes = Cfg::kKVBytes;
   const int h = blockIdx.y;
   pdl_wait();  // q/k/v and the token plan come from earlier kernels
-  const int b = p.order ? p.order[blockIdx.z] : (int)blockIdx.z;
+  const int zb = p.z0 + (int)blockIdx.z;
+  const int b = p.order ? p.order[zb] : zb;
   const int q_begin = p.q_cu[b];
   const int nq = p.q_cu[b + 1] - q_begin;
   const int q_tile0 = blockIdx.x * NT;
@@ -667,13 +669,17 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   kp.dh_out = a.head_dim;
   kp.order = a.order;
   constexpr int kQPerCta = Cfg::NT * kAttnBM;
-  dim3 grid((a.max_q_per_sample + kQPerCta - 1) / kQPerCta, a.H, a.B);
-  if (grid.y > 65535 || grid.z > 65535)
-    return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d or B=%d above 65535", a.H, a.B);
-  cudaError_t e = launch_pdl(attention_tcgen05_kernel<DH, SHORT>, grid, dim3(Cfg::kThreads), Cfg::kSmem, stream,
-                             tq, tk, tv, kp);
-  if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  if (a.H > 65535) return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d above 65535", a.H);
+  // Grid rows are samples; a batch above the 65535-row limit runs as several
+  // launches, each starting at its first row z0.
+  for (int z0 = 0; z0 < a.B; z0 += 65535) {
+    kp.z0 = z0;
+    dim3 grid((a.max_q_per_sample + kQPerCta - 1) / kQPerCta, a.H, a.B - z0 < 65535 ? a.B - z0 : 65535);
+    cudaError_t e = launch_pdl(attention_tcgen05_kernel<DH, SHORT>, grid, dim3(Cfg::kThreads), Cfg::kSmem,
+                               stream, tq, tk, tv, kp);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+  }
   return TJ_OK;
 }
 

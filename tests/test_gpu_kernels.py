@@ -359,6 +359,32 @@ def test_flash_attention_rising_max(cuda_pkg, pattern, causal):
     assert float(err.max()) < 4e-3, float(err.max())
 
 
+def test_flash_attention_more_samples_than_grid_rows(cuda_pkg):
+    """70000 samples (of 1-3 tokens): more than the 65535 rows of one launch's
+    grid, so the library runs it as two launches."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(70000)
+    B, H = 70000, 1
+    lens = torch.randint(1, 4, (B,), generator=g, dtype=torch.int32)
+    cu = torch.zeros(B + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    rows = int(cu[-1])
+    qkv = torch.randn(3, H, rows, 64, generator=g).half()
+    scale = 64**-0.5
+    dev = qkv.to(DEV)
+    out = k.flash_attn_fwd(dev[0], dev[1:2], dev[2:3], cu.to(DEV), cu[:-1].view(-1, 1).contiguous().to(DEV),
+                           lens.view(-1, 1).contiguous().to(DEV), 3, scale).float().cpu()
+    # Reference per length group (every sample of length L at once).
+    ref = torch.zeros(rows, H * 64)
+    q, kk, vv = qkv[0, 0].float(), qkv[1, 0].float(), qkv[2, 0].float()
+    for L in (1, 2, 3):
+        idx = torch.nonzero(lens == L).flatten()
+        rws = (cu[idx].long()[:, None] + torch.arange(L)[None, :])  # [n, L]
+        s = torch.einsum("nid,njd->nij", q[rws], kk[rws]) * scale
+        ref[rws.reshape(-1)] = torch.einsum("nij,njd->nid", torch.softmax(s, -1), vv[rws]).reshape(-1, 64)
+    assert float((out - ref).abs().max()) < 4e-3
+
+
 def test_flash_attention_segments(cuda_pkg):
     """Two key segments per sample (the context-parallel layout [G][H][rows][64])."""
     k = cuda_pkg.kernels

@@ -157,6 +157,16 @@ def test_wide_model(cuda_pkg):
     _gate(oracle.encoder_forward(sd, cfg, x, mask), out, "d_model 5120")
 
 
+def test_batch_above_grid_rows(cuda_pkg):
+    """70000 short sequences: more samples than one launch's attention grid
+    holds (65535 rows), so attention runs in two launches."""
+    cfg = oracle.TransformerConfig(70000, 3, 64, 1, 128, 1, False)
+    sd = oracle.make_state_dict(cfg, seed=31)
+    x, mask = oracle.generate_random_case(cfg, seed=31, padding_ratio=0.5)
+    out = _run(_model(cuda_pkg, cfg, sd), x, mask)
+    _gate(oracle.encoder_forward(sd, cfg, x, mask), out, "B=70000")
+
+
 def test_two_layers_causal(cuda_pkg):
     cfg = oracle.TransformerConfig(2, 640, 256, 4, 1024, 2, True)
     sd = oracle.make_state_dict(cfg, seed=21)
