@@ -11,7 +11,9 @@ from .encoder_oracle import (  # noqa: F401
     compare_outputs,
     encoder_forward,
     encoder_forward_blocked,
+    encoder_forward_query_rows,
     generate_random_case,
+    long_sequence_check_rows,
     make_state_dict,
     perturb_layernorm,
     update_accuracy,

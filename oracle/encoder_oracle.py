@@ -254,6 +254,89 @@ def encoder_forward_blocked(
     return torch.cat(outs, dim=0)
 
 
+@torch.inference_mode()
+def encoder_forward_query_rows(
+    sd, config: TransformerConfig, x: torch.Tensor, mask: Optional[torch.Tensor], rows, query_chunk: int = 64
+) -> torch.Tensor:
+    """Output rows `rows` (sequence positions) of a ONE-layer encoder on ONE
+    sample, without evaluating the other rows.
+
+    The query-blocked oracle (memory_bounded_baseline, tools/shape14/accuracy.py:125-156,
+    attention :68-122) restricted to a subset of query blocks.  Keys and values
+    depend on every token, so LN1 and the K/V projections run over the whole
+    sequence; Q, the attention rows, the out-projection, the residual adds,
+    LN2, the FFN and the final LayerNorm are evaluated for `rows` only (every
+    op except attention is per token, and with one layer the other rows'
+    outputs never feed these).  The formula is the reference's unchanged:
+    scores * scale, causal and key masks as -inf, FP32 softmax, probs @ v,
+    invalid query rows zeroed after attention, after the block and after the
+    final LayerNorm.  Returns [len(rows), D]."""
+    if x.shape[0] != 1:
+        raise ValueError("the query-row oracle evaluates one sample")
+    if config.num_layers != 1:
+        raise ValueError("the query-row oracle needs one layer (later layers read every row)")
+    rows = torch.as_tensor(rows, dtype=torch.int64).reshape(-1)
+    _, S, D = x.shape
+    H = config.num_heads
+    if rows.numel() and (int(rows.min()) < 0 or int(rows.max()) >= S):
+        raise ValueError("query rows out of range")
+    p = "layers.0."
+    a = p + "attention."
+    scale = (D // H) ** -0.5
+    h = F.layer_norm(x, (D,), sd[p + "norm1.weight"], sd[p + "norm1.bias"], 1e-5)
+    k = _split_heads(F.linear(h, sd[a + "k_proj.weight"], sd[a + "k_proj.bias"]), H)
+    v = _split_heads(F.linear(h, sd[a + "v_proj.weight"], sd[a + "v_proj.bias"]), H)
+    q = _split_heads(F.linear(h[:, rows], sd[a + "q_proj.weight"], sd[a + "q_proj.bias"]), H)
+    del h
+    ctx = torch.empty_like(q)
+    key_pos = torch.arange(S, device=x.device)[None, :]
+    invalid_keys = None if mask is None else ~mask[:, None, None, :]
+    kt = k.transpose(-2, -1)
+    for start in range(0, rows.numel(), query_chunk):
+        end = min(start + query_chunk, rows.numel())
+        scores = torch.matmul(q[:, :, start:end], kt)
+        scores.mul_(scale)
+        if config.causal:
+            scores.masked_fill_(key_pos > rows[start:end, None], float("-inf"))
+        if invalid_keys is not None:
+            scores.masked_fill_(invalid_keys, float("-inf"))
+        probs = torch.softmax(scores.float(), dim=-1).to(dtype=x.dtype)
+        ctx[:, :, start:end].copy_(torch.matmul(probs, v))
+        del scores, probs
+    merged = ctx.transpose(1, 2).contiguous().view(1, rows.numel(), D)
+    attn = F.linear(merged, sd[a + "out_proj.weight"], sd[a + "out_proj.bias"])
+    qmask = None if mask is None else mask[:, rows]
+    if qmask is not None:
+        attn = attn.masked_fill(~qmask[..., None], 0)
+    xr = x[:, rows] + attn
+    h2 = F.layer_norm(xr, (D,), sd[p + "norm2.weight"], sd[p + "norm2.bias"], 1e-5)
+    h2 = F.gelu(F.linear(h2, sd[p + "ffn_in.weight"], sd[p + "ffn_in.bias"]), approximate="none")
+    xr = xr + F.linear(h2, sd[p + "ffn_out.weight"], sd[p + "ffn_out.bias"])
+    if qmask is not None:
+        xr = xr.masked_fill(~qmask[..., None], 0)
+    out = F.layer_norm(xr, (D,), sd["final_norm.weight"], sd["final_norm.bias"], 1e-5)
+    if qmask is not None:
+        out = out.masked_fill(~qmask[..., None], 0)
+    return out[0]
+
+
+def long_sequence_check_rows(valid_len: int, seq_len: int, block: int = 256) -> torch.Tensor:
+    """Query rows a long-sequence parity check evaluates: the first, a middle
+    and the last block of `block` valid positions (the shape-#14 accuracy
+    tool's query blocks, tools/shape14/accuracy.py:92-119, at the start,
+    middle and end of the valid prefix), plus the first padded position when
+    there is one."""
+    L = int(valid_len)
+    if L <= 0:
+        return torch.zeros(0, dtype=torch.int64)
+    b = min(block, L)
+    mid = max(0, min(L - b, L // 2 - b // 2))
+    picks = [torch.arange(0, b), torch.arange(mid, mid + b), torch.arange(L - b, L)]
+    if L < seq_len:
+        picks.append(torch.tensor([L]))
+    return torch.unique(torch.cat(picks))
+
+
 # ---------------------------------------------------------------------------
 # Comparator
 # ---------------------------------------------------------------------------

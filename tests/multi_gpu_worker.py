@@ -6,7 +6,10 @@ Checks, on N GPUs over NCCL:
   * context parallelism: one sequence split into valid-token balanced chunks,
     K/V all-gathered every layer; the gathered output passes the reference's
     strict gate against the single-GPU model (non-causal one layer, and
-    causal two layers).
+    causal two layers);
+  * context parallelism at the long-sequence config (B1 S131072 D1024 H16
+    F4096): three 256-row query blocks against the query-row oracle with the
+    strict gate, padded rows exactly zero.
 Exits non-zero on any failure.
 """
 from __future__ import annotations
@@ -85,10 +88,45 @@ def main() -> int:
                 failures.append(f"context parallel {cfg_t}: {r}")
             if torch.count_nonzero(out.cpu()[~mask]) != 0:
                 failures.append(f"context parallel {cfg_t}: padded rows not zero")
+
+        # ---- context parallelism at the long-sequence config ----------------
+        # B1 S131072 D1024 H16 F4096, valid length ~ U[0.9S, S]: every rank
+        # checks its chunk (finite, padded rows exactly zero); the rows of three
+        # 256-row query blocks are summed to rank 0 (each row is owned by one
+        # rank, the others add zeros), which gates them against the query-row
+        # oracle after the process group is gone.
+        cfg = oracle.TransformerConfig(1, 131072, 1024, 16, 4096, 1, False)
+        sd = oracle.make_state_dict(cfg, seed=1234)
+        x, mask = oracle.generate_random_case(cfg, seed=1234, padding_ratio=0.1)
+        model = model_for(cfg, sd)
+        ranges = sharding.sequence_ranges(mask[0], world)
+        slab = max(e - s for s, e in ranges)
+        s0, e0 = ranges[rank]
+        cp = sharding.ContextParallelEncoder(model)
+        out_local = cp.forward(x[:, s0:e0].contiguous().to(dev), mask[:, s0:e0].contiguous().to(dev), slab)[0]
+        if not bool(torch.isfinite(out_local).all()):
+            failures.append("context parallel S=131072: non-finite output")
+        if torch.count_nonzero(out_local[~mask[0, s0:e0].to(dev)]) != 0:
+            failures.append("context parallel S=131072: padded rows not zero")
+        L = int(mask.sum())
+        check_rows = oracle.long_sequence_check_rows(L, cfg.seq_len)
+        picked = torch.zeros(check_rows.numel(), cfg.d_model, device=dev)
+        own = (check_rows >= s0) & (check_rows < e0)
+        picked[own.to(dev)] = out_local[(check_rows[own] - s0).to(dev)]
+        dist.all_reduce(picked)
+        picked = picked.cpu()
+        del model, cp, out_local
         pkg._lib.device_status(torch.cuda.current_stream().cuda_stream)
 
     dist.barrier(device_ids=[local])
     dist.destroy_process_group()
+    if rank == 0:
+        ref = oracle.encoder_forward_query_rows(sd, cfg, x, mask, check_rows)
+        r = oracle.compare_outputs(ref, picked)
+        print(f"context parallel S=131072 over {world} GPUs: {check_rows.numel()} rows, "
+              f"max_abs={r.max_abs_error:.3g}, failed={r.failed_elements}", flush=True)
+        if not r.passed:
+            failures.append(f"context parallel S=131072 against the query-row oracle: {r}")
     if failures:
         print(f"rank {rank} FAILED:\n" + "\n".join(failures), flush=True)
         return 1

@@ -86,6 +86,36 @@ def test_blocked_equals_dense_oracle():
     torch.testing.assert_close(dense, blocked, rtol=0, atol=2e-5)
 
 
+def test_query_row_oracle_matches_reference_blocked_outputs(golden):
+    """The query-row oracle (the long-sequence checker) on the reference's own
+    memory-bounded case: its rows match the reference's stored row sums,
+    sums of squares and first 16 features at those rows."""
+    e = golden["blocked_b1_s2048_d128"]
+    cfg, sd, x, mask = _rebuild(e)
+    rows = oracle.long_sequence_check_rows(int(mask.sum()), cfg.seq_len)
+    assert rows.numel() == 3 * 256 + 1  # three blocks + the first padded row
+    out = oracle.encoder_forward_query_rows(sd, cfg, x, mask, rows).double()
+    torch.testing.assert_close(out.sum(1), e["row_sum"][rows], rtol=1e-6, atol=1e-4)
+    torch.testing.assert_close((out * out).sum(1), e["row_sqsum"][rows], rtol=1e-6, atol=1e-4)
+    torch.testing.assert_close(out[:, :16].float(), e["head"][rows], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("cfg_t,pad", [((1, 1500, 96, 3, 192, 1, True), 0.2),
+                                       ((1, 1024, 64, 2, 128, 1, False), 0.0),
+                                       ((1, 700, 40, 4, 80, 1, False), 0.6)])
+def test_query_row_oracle_equals_blocked_oracle(cfg_t, pad):
+    cfg = oracle.TransformerConfig(*cfg_t)
+    sd = oracle.make_state_dict(cfg, seed=11)
+    x, mask = oracle.generate_random_case(cfg, seed=11, padding_ratio=pad)
+    m = mask if pad > 0 else None
+    full = oracle.encoder_forward_blocked(sd, cfg, x, m, query_chunk=128)[0]
+    rows = oracle.long_sequence_check_rows(int(mask.sum()), cfg.seq_len, block=100)
+    sub = oracle.encoder_forward_query_rows(sd, cfg, x, m, rows)
+    torch.testing.assert_close(sub, full[rows], rtol=0, atol=1e-5)
+    with pytest.raises(ValueError):
+        oracle.encoder_forward_query_rows(sd, oracle.TransformerConfig(1, 10, 40, 4, 80, 2, False), x, m, rows)
+
+
 def test_comparator_is_strict_or():
     ref = torch.tensor([0.01, 0.0, 100.0, float("nan")])
     # abs 0.0025 and rel 25% fail; abs 0.0019 passes; rel 1.9% of 100 passes; NaN fails.
