@@ -242,6 +242,43 @@ TJ_API int tj_encoder_forward(const tj_encoder_desc* desc, const tj_layer_weight
                        const uint8_t* mask, float* out, void* workspace, int64_t workspace_bytes,
                        void* stream);
 
+/* ---- peer exchange (the batch-sharded output gather) --------------------
+ *
+ * The reference runs on one GPU and has no multi-GPU code; its single-GPU
+ * batch split (balanced sample ranges, candidates/v19/parallel_batch_common.py:31-51)
+ * is what these entry points scale out.  A batch split over the GPUs of one
+ * node ends with the output gather: each rank pushes the valid rows of its
+ * finished samples into every rank's [B, S, D] output with the copy engines,
+ * over NVLink, while its next micro-batch computes.  The library does not
+ * allocate: the caller exports its own buffers and maps the peers'. */
+
+#define TJ_IPC_HANDLE_BYTES 64
+
+/* Exports the device allocation that contains `ptr` for the other processes
+ * of this node: handle_out receives TJ_IPC_HANDLE_BYTES bytes and offset_out
+ * the byte offset of ptr inside that allocation (the caller adds it to the
+ * base tj_ipc_open returns in the other process).  The allocation must come
+ * from cudaMalloc (e.g. torch's default caching allocator). */
+TJ_API int tj_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+
+/* Maps a peer's exported allocation into this process, with peer access over
+ * NVLink, and returns its base address; undo with tj_ipc_close. */
+TJ_API int tj_ipc_open(const void* handle, void** base_out);
+
+/* Unmaps an allocation mapped by tj_ipc_open (NULL is a no-op). */
+TJ_API int tj_ipc_close(void* base);
+
+typedef struct tj_copy_segment {
+  void* dst;        /* device address, may be a peer mapping from tj_ipc_open */
+  const void* src;  /* device address; NULL = fill dst with zero bytes */
+  int64_t bytes;
+} tj_copy_segment;
+
+/* Enqueues, in order on `stream`, one asynchronous device-to-device copy (or
+ * zero fill, src == NULL) per segment.  Copies to a peer mapping run on the
+ * copy engines over NVLink; no kernel is launched. */
+TJ_API int tj_copy_segments(const tj_copy_segment* segs, int n, void* stream);
+
 /* ---- encoder without a caller workspace --------------------------------- */
 
 /* Size of the library's static device workspace used by

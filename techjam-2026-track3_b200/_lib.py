@@ -47,6 +47,13 @@ class EncoderDesc(ctypes.Structure):
     ]
 
 
+class CopySegment(ctypes.Structure):
+    _fields_ = [("dst", c_vp), ("src", c_vp), ("bytes", c_i64)]
+
+
+TJ_IPC_HANDLE_BYTES = 64
+
+
 class LayerWeights(ctypes.Structure):
     _fields_ = [
         ("ln1_gamma", c_vp),
@@ -116,6 +123,10 @@ SIGNATURES = {
             c_vp, c_vp, c_i64, c_vp,
         ],
     ),
+    "tj_ipc_export": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),
+    "tj_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "tj_ipc_close": (c_int, [c_vp]),
+    "tj_copy_segments": (c_int, [ctypes.POINTER(CopySegment), c_int, c_vp]),
     "tj_encoder_forward_noalloc": (
         c_int,
         [ctypes.POINTER(EncoderDesc), ctypes.POINTER(LayerWeights), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
@@ -189,3 +200,39 @@ def device_status(stream: int = 0) -> list[int]:
         raise TJError("device_status", rc, last_error())
     check(rc, "device_status")
     return status
+
+
+# ---- peer exchange ------------------------------------------------------------
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """(handle bytes, byte offset of ptr in its allocation) for the peers."""
+    h = ctypes.create_string_buffer(TJ_IPC_HANDLE_BYTES)
+    off = c_i64(0)
+    check(load().tj_ipc_export(c_vp(ptr), h, ctypes.byref(off)), "ipc_export")
+    return h.raw, int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Maps a peer allocation; returns its base address in this process."""
+    if len(handle) != TJ_IPC_HANDLE_BYTES:
+        raise ValueError("IPC handle must be %d bytes" % TJ_IPC_HANDLE_BYTES)
+    base = c_vp()
+    check(load().tj_ipc_open(ctypes.create_string_buffer(handle, TJ_IPC_HANDLE_BYTES), ctypes.byref(base)),
+          "ipc_open")
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    check(load().tj_ipc_close(c_vp(base)), "ipc_close")
+
+
+def copy_segments(segments, stream: int) -> None:
+    """Enqueues (dst, src or 0 for a zero fill, bytes) copies on `stream`."""
+    n = len(segments)
+    if n == 0:
+        return
+    arr = (CopySegment * n)()
+    for i, (dst, src, nbytes) in enumerate(segments):
+        arr[i].dst = dst
+        arr[i].src = src or None
+        arr[i].bytes = nbytes
+    check(load().tj_copy_segments(arr, n, c_vp(stream)), "copy_segments")

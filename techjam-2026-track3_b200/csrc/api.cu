@@ -497,3 +497,5 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
 // Workspace-free variant of tj_encoder_forward (its own file: static device
 // workspace and the per-device address lookup).
 #include "noalloc.cu"
+// Peer-memory plumbing of the batch-sharded output gather.
+#include "exchange.cu"

@@ -7,8 +7,10 @@ One process per GPU (torchrun), torch.distributed for the plumbing.
   (the balanced-range split of the reference's multi-stream variant,
   candidates/v19/parallel_batch_common.py:31-51) or, balanced by estimated
   work rather than count, the sample set of `balanced_assignment`, with no
-  data-path collective; `BatchShardedEncoder.forward(..., gather=True)`
-  optionally all-gathers the outputs (back in batch order).
+  data-path collective in the forward itself; `BatchShardedEncoder.forward(
+  ..., gather=True)` ends with the output gather: copy-engine pushes of the
+  valid rows of every finished micro-batch into every rank's [B, S, D]
+  output over NVLink (peer mappings), overlapped with the next micro-batch.
 * Context parallelism for one long sequence: rank g holds a contiguous chunk
   of the sequence.  Attention is the only op that mixes tokens, so each rank
   computes LN1 and the QKV projection for its own tokens, all-gathers the
@@ -87,19 +89,93 @@ def balanced_assignment(lengths: Sequence[int], world: int, d_model: int, ffn_di
     return [sorted(o) for o in out]
 
 
+def micro_batch_ranges(n: int, parts: int) -> List[Tuple[int, int]]:
+    """Splits n local samples into at most `parts` contiguous micro-batches
+    (sizes differing by at most one, the larger ones first)."""
+    if n <= 0:
+        return []
+    return [r for r in batch_ranges(n, max(1, min(parts, n))) if r[1] > r[0]]
+
+
+def gather_segments(assignment: Sequence[Sequence[int]], rank: int, group: Tuple[int, int], seq_len: int,
+                    row_bytes: int, valid_lengths: Optional[Sequence[int]]) -> List[Tuple[int, int, int]]:
+    """Copies one destination needs for micro-batch `group` = local samples
+    [j0, j1) of `rank`: (byte offset in the [B, S, D] output, byte offset in
+    the micro-batch's [j1-j0, S, D] output, bytes).  With right-padded masks
+    (valid_lengths given) only a sample's valid rows are copied; otherwise the
+    whole sample, its zero rows included."""
+    j0, j1 = group
+    mine = assignment[rank]
+    sample_bytes = seq_len * row_bytes
+    out = []
+    for j in range(j0, j1):
+        b = mine[j]
+        n = sample_bytes if valid_lengths is None else int(valid_lengths[b]) * row_bytes
+        if n > 0:
+            out.append((b * sample_bytes, (j - j0) * sample_bytes, n))
+    return out
+
+
+def zero_fill_segments(valid_lengths: Sequence[int], seq_len: int, row_bytes: int) -> List[Tuple[int, int]]:
+    """(byte offset, bytes) of every sample's padded tail in the [B, S, D]
+    output of a right-padded batch: the rows no rank sends."""
+    out = []
+    for b, L in enumerate(valid_lengths):
+        L = int(L)
+        if not 0 <= L <= seq_len:
+            raise ValueError(f"valid length {L} of sample {b} outside [0, {seq_len}]")
+        if L < seq_len:
+            out.append(((b * seq_len + L) * row_bytes, (seq_len - L) * row_bytes))
+    return out
+
+
+class _Exchange:
+    """A few [B, S, D] fp32 output buffers per rank (used in turn), each mapped
+    into every other rank of the group (CUDA IPC), plus one copy stream per
+    destination."""
+
+    def __init__(self, key, bufs, ptrs, mapped, streams, flag):
+        self.key = key
+        self.bufs = bufs          # this rank's output buffers
+        self.ptrs = ptrs          # ptrs[d][i]: address of rank d's buffer i in this process
+        self.mapped = mapped      # peer allocation bases opened here (closed on release)
+        self.streams = streams    # streams[d]: copies into rank d
+        self.flag = flag          # one-element tensor all-reduced as the completion barrier
+
+
 class BatchShardedEncoder:
     """Runs `model` on this rank's share of the batch: a contiguous range
-    (`local_range`), or the work-balanced sample set of `balanced_assignment`
-    (`local_samples`), in which case `forward(..., gather=True, assignment=a)`
-    puts the gathered outputs back in batch order."""
+    (`local_range`), or the work-balanced sample set of `balanced_assignment`.
 
-    def __init__(self, model, group=None) -> None:
+    forward(..., gather=True) also gathers the [B, S, D] output of the whole
+    batch on every rank.  The samples run in micro-batches; as soon as one
+    micro-batch is finished, the copy engines push the valid rows of its
+    samples into every rank's output buffer over NVLink (peer mappings, no
+    SM time, no padded rows on the link) while the next micro-batch computes.
+    Each rank zero-fills the padded rows of its own buffer, and an all-reduce
+    of one element on the current stream, after this rank's last push, is the
+    barrier after which every rank's buffer is complete.
+
+    The gathered output is one of `buffers` persistent buffers used in turn:
+    the output of call i stays intact until this rank's current stream
+    reaches the end of call i + buffers - 1 (peers start writing a buffer
+    again only after every rank has passed the previous call's barrier);
+    clone it to keep it longer.  Call `close()` (on every rank) before the
+    process group goes away."""
+
+    def __init__(self, model, group=None, micro_batches: int = 2, buffers: int = 2) -> None:
         import torch.distributed as dist
 
         self.model = model
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.micro_batches = max(1, int(micro_batches))
+        if buffers < 2:
+            raise ValueError("the gather needs at least two output buffers")
+        self.buffers = int(buffers)
+        self._exchange: Optional[_Exchange] = None
+        self._turn = 0
 
     def local_range(self, batch: int) -> Tuple[int, int]:
         return batch_ranges(batch, self.world)[self.rank]
@@ -111,27 +187,120 @@ class BatchShardedEncoder:
         return balanced_assignment(lengths, self.world, cfg.d_model, cfg.ffn_dim)
 
     def forward(self, x_local: torch.Tensor, mask_local: Optional[torch.Tensor], gather: bool = False,
-                assignment: Optional[Sequence[Sequence[int]]] = None):
-        # A rank may hold no samples (batch < world); it still joins the gather.
-        out = self.model(x_local, mask_local)
+                assignment: Optional[Sequence[Sequence[int]]] = None,
+                valid_lengths: Optional[Sequence[int]] = None):
+        """x_local [B_r, S, D] holds this rank's samples in the order of
+        `assignment[rank]` (contiguous batch ranges when assignment is None).
+        valid_lengths: per-sample valid counts of the GLOBAL batch when the
+        mask is right-padded (valid tokens first); then only valid rows cross
+        NVLink.  Without it whole samples are copied (any mask)."""
         if not gather or self.world == 1:
-            return out
+            return self.model(x_local, mask_local)  # a rank may hold no samples (batch < world)
+        return self._gather_forward(x_local, mask_local, assignment, valid_lengths)
+
+    # ---- the gather ---------------------------------------------------------
+    def _global_assignment(self, n_local: int, device) -> List[List[int]]:
         import torch.distributed as dist
 
-        sizes = [torch.zeros(1, dtype=torch.int64, device=out.device) for _ in range(self.world)]
-        dist.all_gather(sizes, torch.tensor([out.shape[0]], dtype=torch.int64, device=out.device), group=self.group)
-        sizes = [int(s.item()) for s in sizes]
-        parts = [torch.empty((n,) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device) for n in sizes]
-        dist.all_gather(parts, out.contiguous(), group=self.group)
-        full = torch.cat(parts, 0)
+        sizes = [torch.zeros(1, dtype=torch.int64, device=device) for _ in range(self.world)]
+        dist.all_gather(sizes, torch.tensor([n_local], dtype=torch.int64, device=device), group=self.group)
+        out, start = [], 0
+        for s in sizes:
+            n = int(s.item())
+            out.append(list(range(start, start + n)))
+            start += n
+        return out
+
+    def _exchange_for(self, B: int, S: int, D: int, device) -> _Exchange:
+        import torch.distributed as dist
+
+        from . import _lib
+
+        key = (B, S, D, device)
+        if self._exchange is not None and self._exchange.key == key:
+            return self._exchange
+        self.close()
+        bufs = [torch.empty(B, S, D, dtype=torch.float32, device=device) for _ in range(self.buffers)]
+        mine = [_lib.ipc_export(b.data_ptr()) for b in bufs]
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=self.group)
+        ptrs: List[List[int]] = []
+        mapped = {}
+        for d in range(self.world):
+            if d == self.rank:
+                ptrs.append([b.data_ptr() for b in bufs])
+                continue
+            row = []
+            for handle, offset in every[d]:
+                if handle not in mapped:  # several buffers may share one allocation
+                    mapped[handle] = _lib.ipc_open(handle)
+                row.append(mapped[handle] + offset)
+            ptrs.append(row)
+        streams = [torch.cuda.Stream(device) for _ in range(self.world)]
+        flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self._exchange = _Exchange(key, bufs, ptrs, list(mapped.values()), streams, flag)
+        self._turn = 0
+        return self._exchange
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (collective: every rank calls it, so no
+        rank frees a buffer another still maps)."""
+        ex = self._exchange
+        if ex is None:
+            return
+        import torch.distributed as dist
+
+        from . import _lib
+
+        for s in ex.streams:
+            s.synchronize()
+        torch.cuda.current_stream(ex.flag.device).synchronize()
+        for base in ex.mapped:
+            _lib.ipc_close(base)
+        dist.barrier(group=self.group, device_ids=[ex.flag.device.index])
+        self._exchange = None
+
+    def _gather_forward(self, x_local, mask_local, assignment, valid_lengths):
+        import torch.distributed as dist
+
+        from . import _lib
+
+        dev = x_local.device
+        n_local, S, D = x_local.shape
         if assignment is None:
-            return full
-        order = torch.tensor([i for r in assignment for i in r], dtype=torch.int64, device=full.device)
-        if order.numel() != full.shape[0]:
-            raise ValueError("assignment does not cover the gathered batch")
-        result = torch.empty_like(full)
-        result[order] = full
-        return result
+            assignment = self._global_assignment(n_local, dev)
+        if len(assignment) != self.world or len(assignment[self.rank]) != n_local:
+            raise ValueError("assignment does not match the ranks' local batches")
+        B = sum(len(a) for a in assignment)
+        if valid_lengths is not None and len(valid_lengths) != B:
+            raise ValueError(f"valid_lengths has {len(valid_lengths)} entries for a batch of {B}")
+        ex = self._exchange_for(B, S, D, dev)
+        buf = self._turn
+        self._turn = (self._turn + 1) % self.buffers
+        row_bytes = D * 4
+        compute = torch.cuda.current_stream(dev)
+        if valid_lengths is not None:
+            base = ex.ptrs[self.rank][buf]
+            _lib.copy_segments([(base + off, 0, n) for off, n in zero_fill_segments(valid_lengths, S, row_bytes)],
+                               compute.cuda_stream)
+        for j0, j1 in micro_batch_ranges(n_local, self.micro_batches):
+            out = self.model(x_local[j0:j1], None if mask_local is None else mask_local[j0:j1])
+            done = torch.cuda.Event()
+            done.record(compute)
+            segs = gather_segments(assignment, self.rank, (j0, j1), S, row_bytes, valid_lengths)
+            src = out.data_ptr()
+            for d in range(self.world):
+                stream = ex.streams[d]
+                stream.wait_event(done)
+                dst = ex.ptrs[d][buf]
+                _lib.copy_segments([(dst + do, src + so, n) for do, so, n in segs], stream.cuda_stream)
+                out.record_stream(stream)
+        for stream in ex.streams:
+            compute.wait_stream(stream)
+        # Completes on a rank only after every rank has reached it, i.e. after
+        # every rank's pushes (ordered before it on that rank's stream) landed.
+        dist.all_reduce(ex.flag, group=self.group)
+        return ex.bufs[buf]
 
 
 def segment_metadata(counts: torch.Tensor, rank: int, causal: bool):

@@ -2,7 +2,9 @@
 
 Checks, on N GPUs over NCCL:
   * batch sharding: each rank runs its balanced range of the batch; the
-    gathered output is bit-identical to the whole batch on one GPU;
+    gathered output (copy-engine pushes over NVLink; valid rows only for
+    right-padded masks, whole samples otherwise; 1-3 micro-batches) is
+    bit-identical to the whole batch on one GPU;
   * context parallelism: one sequence split into valid-token balanced chunks,
     K/V all-gathered every layer; the gathered output passes the reference's
     strict gate against the single-GPU model (non-causal one layer, and
@@ -65,6 +67,25 @@ def main() -> int:
         out = bs.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign)
         if not torch.equal(out, full):
             failures.append(f"balanced batch sharding differs from one GPU: {float((out - full).abs().max())}")
+        # right-padded masks: only valid rows cross NVLink, padded rows zero-filled
+        # by the receiver; one to three micro-batches per rank, and twice in a
+        # row so both exchange buffers (with the other call's stale rows) are used
+        lengths = mask.sum(1).tolist()
+        for mb in (1, 3):
+            bs.micro_batches = mb
+            for rep in range(2):
+                out = bs.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign,
+                                 valid_lengths=lengths)
+                if not torch.equal(out, full):
+                    failures.append(f"valid-row gather (micro-batches {mb}, call {rep}) differs from one GPU")
+        # a non-prefix mask: whole samples are copied
+        mask2 = mask.clone()
+        mask2[:, 1::3] = False
+        full2 = model(x.to(dev), mask2.to(dev))
+        out = bs.forward(x[mine].to(dev), mask2[mine].to(dev), gather=True, assignment=assign)
+        if not torch.equal(out, full2):
+            failures.append("whole-sample gather of a non-prefix mask differs from one GPU")
+        bs.close()
 
         # ---- context parallelism -------------------------------------------
         for cfg_t, pad in (((1, 4096, 1024, 16, 4096, 1, False), 0.1), ((1, 3000, 512, 8, 1024, 2, True), 0.2)):

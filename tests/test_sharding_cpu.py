@@ -52,6 +52,42 @@ def test_balanced_assignment(pkg, world):
         assert worst <= worst_ranges + 1e-6
 
 
+@pytest.mark.parametrize("world,micro", [(2, 1), (3, 2), (4, 3), (8, 2)])
+@pytest.mark.parametrize("prefix", [True, False])
+def test_gather_plan_rebuilds_the_batch_output(pkg, world, micro, prefix):
+    """The output gather's copy plan, replayed on CPU byte arrays: every
+    rank's pushes of its micro-batches (gather_segments) plus the receiver's
+    zero fill (zero_fill_segments, right-padded masks) rebuild the full
+    [B, S, D] output exactly, over a buffer holding a previous call's rows."""
+    from techjam_b200 import sharding
+
+    g = torch.Generator().manual_seed(world * 10 + micro)
+    B, S, D = 13, 9, 3
+    row = D * 4
+    lengths = torch.randint(0, S + 1, (B,), generator=g).tolist()
+    full = torch.randn(B, S, D, generator=g)
+    for b, n in enumerate(lengths):
+        full[b, n:] = 0  # padded rows of the model's output are zero
+    assign = sharding.balanced_assignment(lengths, world, 64, 256)
+    dest = torch.randn(B, S, D, generator=g)  # stale rows of an earlier call
+    d_bytes = dest.view(-1).view(torch.uint8)
+    if prefix:
+        for off, n in sharding.zero_fill_segments(lengths, S, row):
+            d_bytes[off : off + n] = 0
+    for r in range(world):
+        mine = assign[r]
+        local = full[torch.tensor(mine, dtype=torch.int64)] if mine else torch.zeros(0, S, D)
+        for j0, j1 in sharding.micro_batch_ranges(len(mine), micro):
+            src = local[j0:j1].contiguous().view(-1).view(torch.uint8)
+            for do, so, n in sharding.gather_segments(assign, r, (j0, j1), S, row, lengths if prefix else None):
+                d_bytes[do : do + n] = src[so : so + n]
+    assert torch.equal(dest, full)
+    with pytest.raises(ValueError):
+        sharding.zero_fill_segments([S + 1], S, row)
+    assert sharding.micro_batch_ranges(0, 2) == []
+    assert sharding.micro_batch_ranges(5, 2) == [(0, 3), (3, 5)]
+
+
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_sequence_ranges_balance_valid_tokens(pkg, world):
     from techjam_b200 import sharding
