@@ -2,29 +2,41 @@
 """Throughput benchmark of the B200 encoder layer (UserOptimizedTransformer.forward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dense|short|batch|long]
+                    [--workload batch|dense|short|long|refN]
 
 Metric: layer-forward tokens/s = B*S / step time (padded tokens counted, the
-reference's definition, torch_transformer_benchmark.py:565-567).  A step is
-one forward of one synthetic batch already resident in HBM.  Default workload
-(`dense`): B=8, S=2048, d_model=1024, 16 heads, FFN 4096, one layer,
-non-causal, right-padded mask with lengths ~ U[1024, 2048], LayerNorm
-gamma ~ 1+0.02N(0,1), beta ~ 0.02N(0,1), seeded default-init weights.
+reference's definition, torch_transformer_benchmark.py:565-567), whole job.
 
-Multi-GPU (torchrun, one rank per GPU): batch sharding with no data-path
-collective.  `dense` (and `short`): each rank runs its own batch (weak
-scaling).  `batch`: one global batch of 32 sequences split evenly over the
-ranks (strong scaling), the output all-gather timed separately.  `long`: one
-sequence sharded over the ranks (context parallel).  The step time is the
+Default workload (`batch`): one global batch of B=32 sequences of S=4096,
+d_model=1024, 16 heads, FFN 4096, one layer, non-causal, right-padded mask
+with lengths ~ U[1024, 4096], LayerNorm gamma ~ 1+0.02N(0,1), beta ~
+0.02N(0,1), seeded default-init weights.  The batch is split over the N
+ranks (one process per GPU, torchrun, NCCL), B/N samples each balanced by
+work; a step is the forward of every rank's share AND the output gather
+(every rank ends with the [B, S, D] output: copy-engine pushes of valid rows
+over NVLink, overlapped with the next micro-batch), timed together, so the
+curve over N is strong scaling with the gather inside.  The step time is the
 max over ranks of the CUDA-event time of the K timed steps.
 
+The same JSON line nests, measured in the same run at the same N:
+  dense_b8_s2048     the single-GPU dense layer (B=8 S=2048, lengths U[S/2,S])
+                     per rank (weak scaling), with its attention roofline;
+  context_parallel   one sequence of S=131072 (lengths U[0.9S, S]) over the
+                     N ranks (context parallel; the plain model at N=1), with
+                     peak memory per GPU;
+  sustained          >= 3 s of back-to-back headline steps with the SM clock
+                     sampled, against the sustained tensor peak.
+Every timed workload except the long sequence is first gated against the CPU
+FP32 oracle on one sample of the timed input (the reference's strict gate); a
+failure stops the run before any timing (torch_transformer_benchmark.py:725-728).
+
 Rank 0 prints one JSON line.  `--impl reference` times the reference's CPU
-FP32 path (the oracle restatement of BaselineTransformer) on the host cores.
+FP32 path (the oracle restatement of BaselineTransformer) on the host cores,
+rotating through the samples of the same batch.
 """
 from __future__ import annotations
 
 import argparse
-import ctypes
 import json
 import math
 import os
@@ -42,10 +54,10 @@ sys.path.insert(0, str(ROOT))
 
 WORKLOADS = {
     # name: (B, S, D, H, F, layers, causal, padding_ratio, ln_perturb, description)
-    "dense": (8, 2048, 1024, 16, 4096, 1, False, 0.5, True,
-              "dense encoder layer B=8 S=2048 d_model=1024 H=16 FFN=4096, L~U[S/2,S]"),
     "batch": (32, 4096, 1024, 16, 4096, 1, False, 0.75, True,
               "batch-sharded encoder layer B=32 S=4096 d_model=1024 H=16 FFN=4096, L~U[S/4,S]"),
+    "dense": (8, 2048, 1024, 16, 4096, 1, False, 0.5, True,
+              "dense encoder layer B=8 S=2048 d_model=1024 H=16 FFN=4096, L~U[S/2,S]"),
     "short": (64, 128, 768, 12, 3072, 1, False, 0.999, False,
               "short-sequence heavy-padding layer B=64 S=128 d_model=768 H=12 FFN=3072, L~U[1,S]"),
     "long": (1, 131072, 1024, 16, 4096, 1, False, 0.1, False,
@@ -66,6 +78,10 @@ for _sid, _b, _d, _h, _s, _l, _f in REFERENCE_SHAPES:
                                f"reference official shape #{_sid}: B={_b} S={_s} d_model={_d} H={_h} "
                                f"FFN={_f} layers={_l} causal, no padding")
 
+# Workloads whose global batch is split over the ranks (strong scaling, output gather timed).
+SPLIT_BATCH = ("batch",)
+TIMING_SEED = 1234 + 100000  # timing inputs use seed + 100000 (torch_transformer_benchmark.py:533)
+
 PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -75,6 +91,14 @@ def load_peaks():
         d = json.loads(p.read_text())
         return d, "measured"
     return PEAK_FALLBACK, "fallback"
+
+
+def workload_config(workload):
+    """The `config` object of the JSON line (the same in both arms)."""
+    B, S, D, H, F, L, causal, pad, ln, desc = WORKLOADS[workload]
+    min_valid = S if pad <= 0 else max(1, int(round(S * (1.0 - pad))))
+    return {"workload": desc, "global_batch": B, "seq_len": S, "d_model": D, "heads": H, "ffn_dim": F,
+            "layers": L, "causal": causal, "valid_lengths": f"U[{min_valid}, {S}]", "seed": TIMING_SEED}
 
 
 # ---------------------------------------------------------------------------
@@ -106,14 +130,26 @@ def barrier(world, device=None):
             dist.barrier()
 
 
-def max_over_ranks(world, value, device):
+def reduce_over_ranks(world, value, device, op="max"):
     if world == 1:
         return value
     import torch.distributed as dist
 
-    t = torch.tensor([value], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN, "sum": dist.ReduceOp.SUM}[op])
     return float(t.item())
+
+
+def gather_to_all(world, values, device):
+    """List of every rank's `values` (a flat list of floats), by rank."""
+    if world == 1:
+        return [list(values)]
+    import torch.distributed as dist
+
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [p.tolist() for p in parts]
 
 
 # ---------------------------------------------------------------------------
@@ -123,6 +159,7 @@ class ClockSampler:
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
@@ -139,6 +176,7 @@ class ClockSampler:
             )
         except (OSError, FileNotFoundError):
             self.proc = None
+        return self
 
     def stop(self):
         if self.proc is None:
@@ -152,8 +190,7 @@ class ClockSampler:
         self.file.seek(0)
         rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
         os.unlink(self.file.name)
-        sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sms, maxes, power, reasons = [], [], [], {}
         for r in rows:
             try:
                 sm = float(r[1])
@@ -162,56 +199,66 @@ class ClockSampler:
                 continue
             sms.append(sm)
             maxes.append(mx)
-            for n, v in zip(names, r[5:9]):
+            try:
+                power.append(float(r[3]))
+            except (ValueError, IndexError):
+                pass
+            for n, v in zip(self.REASONS, r[5:9]):
                 if v.strip().lower() == "active":
-                    reasons.add(n)
+                    reasons[n] = reasons.get(n, 0) + 1
         if not sms:
             return None
         loaded = [s for s in sms if s > 0.5 * max(sms)]
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
-                "samples": len(sms)}
+                "reason_samples": reasons, "samples": len(sms), "power_w_max": max(power) if power else None}
 
 
 # ---------------------------------------------------------------------------
 # Workload construction
 # ---------------------------------------------------------------------------
-# Workloads whose global batch is split over the ranks (strong scaling).
-SPLIT_BATCH = ("batch",)
+class Case:
+    """One rank's view of a workload: the global batch, the work-balanced
+    assignment (split workloads), this rank's share and the parameters."""
 
+    def __init__(self, workload, rank, world):
+        import oracle
 
-def build_case(workload, rank, device, world=1):
-    """Config, weights and this rank's input.  Split-batch workloads draw one
-    global batch and return rank `rank`'s contiguous 1/world of it; the others
-    draw a batch per rank."""
-    import oracle
-
-    B, S, D, H, F, L, causal, pad, ln, _ = WORKLOADS[workload]
-    cfg = oracle.TransformerConfig(B, S, D, H, F, L, causal)
-    sd = oracle.make_state_dict(cfg, seed=1234)
-    if ln:
-        sd = oracle.perturb_layernorm(sd, 1234)
-    # Timing inputs use seed + 100000 as the reference harness does
-    # (torch_transformer_benchmark.py:533).
-    if workload in SPLIT_BATCH:
-        if B % world != 0:
-            raise SystemExit(f"--workload {workload}: batch {B} does not split over {world} GPUs")
-        x, mask = oracle.generate_random_case(cfg, seed=1234 + 100000, padding_ratio=pad)
-        if world > 1:
-            # B/world samples per rank, balanced by work (sharding.balanced_assignment).
+        B, S, D, H, F, L, causal, pad, ln, _ = WORKLOADS[workload]
+        self.workload = workload
+        self.split = workload in SPLIT_BATCH
+        self.cfg_global = oracle.TransformerConfig(B, S, D, H, F, L, causal)
+        sd = oracle.make_state_dict(self.cfg_global, seed=1234)
+        self.sd = oracle.perturb_layernorm(sd, 1234) if ln else sd
+        seed = TIMING_SEED if self.split else TIMING_SEED + 7919 * rank  # weak scaling: a batch per rank
+        self.x, self.mask = oracle.generate_random_case(self.cfg_global, seed=seed, padding_ratio=pad)
+        self.lengths = self.mask.to(torch.int64).sum(1).tolist()
+        self.right_padded = bool(all(bool(self.mask[b, :n].all()) for b, n in enumerate(self.lengths)))
+        if self.split and world > 1:
+            if B % world != 0:
+                raise SystemExit(f"--workload {workload}: batch {B} does not split over {world} GPUs")
             from techjam_b200 import sharding
 
-            lengths = mask.to(torch.int64).sum(1).tolist()
-            mine = torch.tensor(sharding.balanced_assignment(lengths, world, D, F)[rank], dtype=torch.int64)
-            x, mask = x[mine].contiguous(), mask[mine].contiguous()
-            cfg = oracle.TransformerConfig(B // world, S, D, H, F, L, causal)
-        return cfg, sd, x, mask
-    x, mask = oracle.generate_random_case(cfg, seed=1234 + 100000 + 7919 * rank, padding_ratio=pad)
-    return cfg, sd, x, mask
+            self.assignment = sharding.balanced_assignment(self.lengths, world, D, F)
+            self.mine = self.assignment[rank]
+        else:
+            self.assignment = [list(range(B))] if self.split else None
+            self.mine = list(range(B))
+        idx = torch.tensor(self.mine, dtype=torch.int64)
+        self.x_local = self.x[idx].contiguous()
+        self.mask_local = self.mask[idx].contiguous()
+        self.cfg_local = oracle.TransformerConfig(len(self.mine), S, D, H, F, L, causal)
+
+    def model(self, pkg, device):
+        c = self.cfg_global
+        m = pkg.UserOptimizedTransformer(pkg.TransformerConfig(*c.__dict__.values()))
+        m.load_state_dict(self.sd, strict=True)
+        return m.to(device).eval()
 
 
-def algorithmic_work(cfg, mask):
-    """Valid-token FLOPs of one layer forward and per-kernel units."""
-    lens = mask.sum(1).double()
+def algorithmic_work(cfg, lengths):
+    """Valid-token FLOPs of one layer forward over samples of these lengths:
+    (valid tokens, GEMM FLOPs, attention FLOPs)."""
+    lens = torch.tensor(lengths, dtype=torch.float64)
     D, F = cfg.d_model, cfg.ffn_dim
     nv = float(lens.sum())
     attn = float((4.0 * lens * lens * D).sum())  # QK^T + PV
@@ -221,234 +268,299 @@ def algorithmic_work(cfg, mask):
     return nv, gemm * cfg.num_layers, attn * cfg.num_layers
 
 
+def accuracy_gate(out, case, sample, what, world):
+    """The reference refuses to benchmark an implementation that fails its
+    accuracy check (torch_transformer_benchmark.py:725-728): output row
+    `sample` of the timed input against the CPU FP32 oracle, strict gate."""
+    import oracle
+
+    threads = torch.get_num_threads()
+    torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
+    try:
+        c = case.cfg_global
+        one = oracle.TransformerConfig(1, c.seq_len, c.d_model, c.num_heads, c.ffn_dim, c.num_layers, c.causal)
+        xs, ms = case.x[sample : sample + 1], case.mask[sample : sample + 1]
+        if c.seq_len > 8192:
+            ref = oracle.encoder_forward_blocked(case.sd, one, xs, ms, query_chunk=512)
+        else:
+            ref = oracle.encoder_forward(case.sd, one, xs, ms)
+        r = oracle.compare_outputs(ref, out.detach().float().cpu().view_as(ref))
+    finally:
+        torch.set_num_threads(threads)
+    return {"what": what, "sample": sample, "passed": r.passed, "failed_elements": r.failed_elements,
+            "max_abs_error": r.max_abs_error}
+
+
+def fail_on_gate(world, device, gate):
+    ok = reduce_over_ranks(world, 1.0 if gate["passed"] else 0.0, device, op="min")
+    if ok < 1.0:
+        raise SystemExit(f"accuracy gate failed, refusing to time: {gate}")
+
+
+def timed(fn, steps, world, device, sample_clocks=True, local=0):
+    """Device time (ms, max over ranks) of `steps` calls of fn, bracketed by
+    barrier + synchronize on both sides; nvidia-smi clocks sampled meanwhile."""
+    stream = torch.cuda.current_stream(device)
+    sampler = ClockSampler(local).start() if sample_clocks else None
+    if sampler is not None:
+        time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world, device)
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for i in range(steps):
+        fn(i)
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    clocks = sampler.stop() if sampler is not None else None
+    ms_local = start.elapsed_time(end)
+    return reduce_over_ranks(world, ms_local, device), ms_local, clocks
+
+
 # ---------------------------------------------------------------------------
 # Our arm
 # ---------------------------------------------------------------------------
-def run_context_parallel(args, world, rank, local):
-    """One long sequence sharded over the ranks (strong scaling): valid-token
-    balanced chunks, K/V all-gathered over NCCL every layer."""
-    import __graft_entry__
-
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    init_dist(world, "nccl")
-    pkg = __graft_entry__.load_package()
-    from techjam_b200 import sharding
-
-    cfg, sd, x_cpu, mask_cpu = build_case(args.workload, 0, device)  # same sequence on every rank
-    S, D = cfg.seq_len, cfg.d_model
-    ranges = sharding.sequence_ranges(mask_cpu[0], world)
-    a, b = ranges[rank]
-    slab = max(e - s for s, e in ranges)
-    model = pkg.UserOptimizedTransformer(pkg.TransformerConfig(*cfg.__dict__.values()))
-    model.load_state_dict(sd, strict=True)
-    model = model.to(device).eval()
-    cp = sharding.ContextParallelEncoder(model)
-    x = x_cpu[:, a:b].contiguous().to(device)
-    m = mask_cpu[:, a:b].contiguous().to(device)
-    stream = torch.cuda.current_stream(device)
-    torch.cuda.reset_peak_memory_stats(device)
-    with torch.inference_mode():
-        for _ in range(args.warmup):
-            cp.forward(x, m, slab)
-        torch.cuda.synchronize(device)
-        sampler = ClockSampler(local)
-        sampler.start()
-        time.sleep(0.3)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world, device)
-        torch.cuda.synchronize(device)
-        start.record(stream)
-        for _ in range(args.steps):
-            cp.forward(x, m, slab)
-        end.record(stream)
-        torch.cuda.synchronize(device)
-        barrier(world, device)
-        clocks = sampler.stop()
-    ms_step = max_over_ranks(world, start.elapsed_time(end), device) / args.steps
-    peak_gib = max_over_ranks(world, torch.cuda.max_memory_allocated(device) / 2**30, device)
-    nv, gemm_flops, attn_flops = algorithmic_work(cfg, mask_cpu)
-    line = None
-    if rank == 0:
-        line = {
-            "metric": "layer-forward tokens/s",
-            "value": S / (ms_step / 1e3),
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms_step,
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "fp16 operands, fp32 accumulate/LayerNorm/residual/output",
-            "data": "synthetic (seeded N(0,1) input, default-init weights, right-padded mask)",
-            "config": {
-                "workload": WORKLOADS[args.workload][-1],
-                "global_batch": 1,
-                "seq_len": S,
-                "parallelism": f"context-parallel x{world} (valid-token balanced chunks, NCCL all-gather of K/V)",
-                "valid_tokens": int(nv),
-                "chunk_ranges": ranges,
-            },
-            "tflops_valid": (gemm_flops + attn_flops) / (ms_step / 1e3) / 1e12,
-            "peak_memory_gib_per_gpu": peak_gib,
-            "gpu_launches": (1 + 7 * cfg.num_layers + 1) * args.steps,
-            "clocks": clocks,
-        }
-    import torch.distributed as dist
-
-    dist.barrier(device_ids=[device.index])
-    dist.destroy_process_group()
-    return line
-
-
 def run_ours(args, world, rank, local):
     import __graft_entry__
 
-    if args.workload == "long" and world > 1:
-        return run_context_parallel(args, world, rank, local)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     init_dist(world, "nccl")
     pkg = __graft_entry__.load_package()
-    split = args.workload in SPLIT_BATCH
-    cfg, sd, x_cpu, mask_cpu = build_case(args.workload, rank, device, world)
-    B, S, D = cfg.batch_size, cfg.seq_len, cfg.d_model
-    model = pkg.UserOptimizedTransformer(pkg.TransformerConfig(*cfg.__dict__.values()))
-    model.load_state_dict(sd, strict=True)
-    model = model.to(device).eval()
-    mask = mask_cpu.to(device)
-    # Inputs larger than L2 between timed steps: x rotates over buffers whose
-    # total exceeds the 126 MB L2 (and every step writes ~1 GB of activations).
-    x_bytes = x_cpu.numel() * 4
-    big = x_bytes > 2**31  # one input alone dwarfs L2; skip the extra copies and side measurements
-    n_rot = 1 if big else max(2, math.ceil(256e6 / x_bytes))
-    xs = [x_cpu.to(device) for _ in range(n_rot)]
-    stream = torch.cuda.current_stream(device)
+    try:
+        if args.workload == "long":
+            line = measure_long(pkg, args, world, rank, local, device, headline=True)
+        else:
+            line = measure_headline(pkg, args, world, rank, local, device)
+            if args.workload == "batch" and not args.no_extras:
+                dense = measure_headline(pkg, argparse.Namespace(**{**vars(args), "workload": "dense"}), world,
+                                         rank, local, device, nested=True)
+                cp = measure_long(pkg, args, world, rank, local, device, headline=False)
+                if rank == 0:
+                    line["dense_b8_s2048"] = dense
+                    line["context_parallel"] = cp
+    finally:
+        if world > 1:
+            import torch.distributed as dist
 
-    with torch.inference_mode():
-        for i in range(args.warmup):
-            model(xs[i % n_rot], mask)
-        torch.cuda.synchronize(device)
-        pkg._lib.device_status(stream.cuda_stream)
-
-        sampler = ClockSampler(local)
-        sampler.start()
-        time.sleep(0.3)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world, device)
-        torch.cuda.synchronize(device)
-        start.record(stream)
-        for i in range(args.steps):
-            model(xs[i % n_rot], mask)
-        end.record(stream)
-        torch.cuda.synchronize(device)
-        barrier(world, device)
-        clocks = sampler.stop()
-        ms_total = start.elapsed_time(end)
-        pkg._lib.device_status(stream.cuda_stream)
-    ms_total = max_over_ranks(world, ms_total, device)
-    ms_step = ms_total / args.steps
-    tokens_per_step = B * S * world
-    value = tokens_per_step / (ms_step / 1e3)
-
-    gather = measure_output_gather(model, xs[0], mask, device, world) if split and world > 1 else None
-    e2e = {"unavailable": "input larger than 2 GiB"} if big else measure_e2e(model, x_cpu, mask_cpu, device, args, world)
-    kernels = None if big else kernel_breakdown(pkg, model, cfg, xs[0], mask, device, args)
-    nv, gemm_flops, attn_flops = algorithmic_work(cfg, mask_cpu)
-
-    line = None
-    if rank == 0:
-        peaks, peak_kind = load_peaks()
-        roof = roofline(kernels, peaks, peak_kind) if kernels else None
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            cpu = ({"unavailable": "the FP32 oracle needs hours on the host for this shape"}
-                   if cfg.seq_len > 8192 or cfg.batch_size * cfg.seq_len > 1_000_000
-                   else cpu_baseline(args.workload, budget_s=args.cpu_budget))
-        line = {
-            "metric": "layer-forward tokens/s",
-            "value": value,
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms_step,
-            "higher_is_better": True,
-            "scaling": "strong" if split else "weak",
-            "vs_baseline": None,
-            "dtype": "fp16 operands, fp32 accumulate/LayerNorm/residual/output",
-            "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
-            "config": {
-                "workload": WORKLOADS[args.workload][-1],
-                "global_batch": B * world,
-                "seq_len": S,
-                "d_model": D,
-                "heads": cfg.num_heads,
-                "ffn_dim": cfg.ffn_dim,
-                "layers": cfg.num_layers,
-                "parallelism": (f"batch-sharded x{world}: the global batch split evenly (equal sample counts, "
-                                "balanced by work), output all-gather timed apart (output_gather)"
-                                if split and world > 1
-                                else f"batch-sharded x{world} (no data-path collective)"),
-                "valid_tokens_per_gpu": int(nv),
-                "l2": f"inputs larger than L2: x rotates over {n_rot} buffers of {x_bytes / 2**20:.0f} MiB; "
-                      "each step writes ~1 GB of activations",
-            },
-            "tflops_valid": (gemm_flops + attn_flops) * world / (ms_step / 1e3) / 1e12,
-            "e2e": e2e,
-            "gpu_launches": (2 + 7 * cfg.num_layers) * args.steps,
-            "roofline": roof,
-            "kernels": kernels,
-            "clocks": clocks,
-            "cpu_baseline": cpu,
-        }
-        if gather is not None:
-            gather["value_with_gather"] = tokens_per_step / ((ms_step + gather["ms"]) / 1e3)
-            line["output_gather"] = gather
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier(device_ids=[device.index])
-        dist.destroy_process_group()
+            dist.barrier(device_ids=[device.index])
+            dist.destroy_process_group()
     return line
 
 
-def measure_output_gather(model, x, mask, device, world):
-    """The split batch's only collective: all-gather of every rank's fp32
-    output [B/world, S, D] into the full [B, S, D] on every rank (NCCL over
-    NVLink), timed on the device (max over ranks) over a few repeats."""
-    import torch.distributed as dist
+def measure_headline(pkg, args, world, rank, local, device, nested=False):
+    from techjam_b200 import sharding
+
+    case = Case(args.workload, rank, world)
+    cfg = case.cfg_global
+    B, S = cfg.batch_size, cfg.seq_len
+    model = case.model(pkg, device)
+    encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches)
+    gather = case.split and world > 1
+    lengths = case.lengths if case.right_padded else None
+    mask_local = case.mask_local.to(device)
+    # Inputs larger than L2 between timed steps: x rotates over buffers whose
+    # total exceeds the 126 MB L2 (and every step writes ~1 GB of activations).
+    x_bytes = max(1, case.x_local.numel() * 4)
+    big = x_bytes > 2**31
+    n_rot = 1 if (big or x_bytes >= 256e6) else max(2, math.ceil(256e6 / x_bytes))
+    xs = [case.x_local.to(device) for _ in range(n_rot)]
+
+    def step(i):
+        if gather:
+            return encoder.forward(xs[i % n_rot], mask_local, gather=True, assignment=case.assignment,
+                                   valid_lengths=lengths)
+        return model(xs[i % n_rot], mask_local)
 
     with torch.inference_mode():
-        out = model(x, mask)
-        full = torch.empty((world * out.shape[0],) + tuple(out.shape[1:]), dtype=out.dtype, device=device)
-        for _ in range(2):
-            dist.all_gather_into_tensor(full, out)
+        for i in range(args.warmup):
+            out = step(i)
         torch.cuda.synchronize(device)
-        barrier(world, device)
-        reps = 5
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(reps):
-            dist.all_gather_into_tensor(full, out)
-        end.record()
-        torch.cuda.synchronize(device)
-    ms = max_over_ranks(world, start.elapsed_time(end) / reps, device)
-    return {"ms": ms, "bytes_per_rank": out.numel() * out.element_size(),
-            "collective": "all_gather_into_tensor (NCCL)"}
+        pkg._lib.device_status(torch.cuda.current_stream(device).cuda_stream)
+        # accuracy gate on the timed input: at N>1 a sample another rank computed
+        if case.split:
+            owner = (rank + 1) % world
+            sample = (case.assignment[owner] or case.mine or [0])[0]
+            row = out[sample] if gather else out[case.mine.index(sample)]
+        else:
+            sample, row = 0, out[0]
+        gate = accuracy_gate(row, case, sample, args.workload, world)
+        fail_on_gate(world, device, gate)
+        del out, row
+
+        ms_total, ms_local, clocks = timed(step, args.steps, world, device, local=local)
+        pkg._lib.device_status(torch.cuda.current_stream(device).cuda_stream)
+    ms_step = ms_total / args.steps
+    tokens_per_step = B * S * (1 if case.split else world)
+    value = tokens_per_step / (ms_step / 1e3)
+    nv_local, _, _ = algorithmic_work(cfg, [case.lengths[j] for j in case.mine])
+    per_rank = gather_to_all(world, [len(case.mine), nv_local, ms_local / args.steps], device)
+    nv_all, gemm_f, attn_f = algorithmic_work(cfg, case.lengths)
+    flops_step = (gemm_f + attn_f) * (1 if case.split else world)
+
+    sustained = None
+    if not nested and not args.no_extras:
+        sustained = measure_sustained(step, ms_step, world, device, local, flops_step)
+    e2e = None if big else measure_e2e(case, model, device, args, world, gather, lengths)
+    kernels = kernel_breakdown(pkg, model, case, device, args) if (rank == 0 and not big) else None
+    if gather:
+        encoder.close()
+
+    if rank != 0:
+        return None
+    peaks, peak_kind = load_peaks()
+    roof = roofline(kernels, peaks, peak_kind, args.workload) if kernels else None
+    line = {
+        "metric": "layer-forward tokens/s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong" if case.split else "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 operands, fp32 accumulate/LayerNorm/residual/output",
+        "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
+        "config": workload_config(args.workload),
+        "parallelism": (f"batch split x{world}: {B // world} samples per GPU balanced by work; the step includes "
+                        "the output gather (valid rows pushed by the copy engines over NVLink into every "
+                        f"GPU's [B,S,D] output, {args.micro_batches} micro-batches overlapping it)"
+                        if gather else
+                        (f"batch split x{world}" if case.split else
+                         f"x{world}: each GPU runs its own batch of {B} (weak scaling, no collective)")),
+        "l2_policy": (f"inputs larger than L2: x rotates over {n_rot} buffer(s) of {x_bytes / 2**20:.0f} MiB; "
+                      "each step writes ~1 GB or more of activations"),
+        "valid_tokens": int(nv_all) * (1 if case.split else world),
+        "ranks": [{"rank": r, "samples": int(p[0]), "valid_tokens": int(p[1]), "ms_per_step": p[2]}
+                  for r, p in enumerate(per_rank)],
+        "tflops_valid": flops_step / (ms_step / 1e3) / 1e12,
+        "accuracy_gate": gate,
+        "gpu_launches": launches_per_step(case, gather, args.micro_batches) * args.steps,
+        "roofline": roof,
+        "kernels": kernels,
+        "clocks": clocks,
+        "e2e": e2e,
+        "sustained": sustained,
+    }
+    if not nested:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(args.workload, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = cpu
+    return line
 
 
-def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
+def launches_per_step(case, gather, micro_batches):
+    """Our kernels per step: per forward the token plan, 7 per layer and the
+    final LayerNorm (the gather's copies run on the copy engines)."""
+    from techjam_b200 import sharding
+
+    L = case.cfg_global.num_layers
+    forwards = len(sharding.micro_batch_ranges(len(case.mine), micro_batches)) if gather else (1 if case.mine else 0)
+    return forwards * (2 + 7 * L)
+
+
+def measure_sustained(step, ms_step, world, device, local, flops_step):
+    """>= 3 s of back-to-back steps: the throughput a long run holds once the
+    GPU sits at its power cap, with the SM clock sampled meanwhile."""
+    n = max(10, int(math.ceil(3000.0 / max(ms_step, 1e-3))))
+    with torch.inference_mode():
+        ms_total, _, clocks = timed(step, n, world, device, local=local)
+    peaks, kind = load_peaks()
+    ms = ms_total / n
+    tflops = flops_step / (ms / 1e3) / 1e12
+    sus = peaks.get("bf16_tflops_sustained", PEAK_FALLBACK["bf16_tflops_sustained"])
+    return {"steps": n, "seconds": ms_total / 1e3, "ms_per_step": ms, "tflops_valid": tflops,
+            "frac_of_sustained_peak": tflops / sus, "sustained_peak_tflops": sus, "peak_source": kind,
+            "clocks": clocks}
+
+
+def measure_long(pkg, args, world, rank, local, device, headline):
+    """One sequence of S=131072 (lengths U[0.9S, S]): context parallel over the
+    ranks (valid-token balanced chunks, K/V all-gathered over NCCL every
+    layer); at N=1 the plain model.  Peak memory per GPU reported."""
+    from techjam_b200 import sharding
+
+    case = Case("long", 0, 1)  # the same sequence on every rank
+    cfg = case.cfg_global
+    S = cfg.seq_len
+    model = case.model(pkg, device)
+    steps = args.steps if headline else max(3, min(args.steps, 10))
+    warm = args.warmup if headline else 3
+    torch.cuda.synchronize(device)
+    torch.cuda.reset_peak_memory_stats(device)
+    if world > 1:
+        ranges = sharding.sequence_ranges(case.mask[0], world)
+        a, b = ranges[rank]
+        slab = max(e - s for s, e in ranges)
+        cp = sharding.ContextParallelEncoder(model)
+        x = case.x[:, a:b].contiguous().to(device)
+        m = case.mask[:, a:b].contiguous().to(device)
+        fn = lambda i: cp.forward(x, m, slab)  # noqa: E731
+    else:
+        ranges = [(0, S)]
+        x = case.x.to(device)
+        m = case.mask.to(device)
+        fn = lambda i: model(x, m)  # noqa: E731
+    with torch.inference_mode():
+        for i in range(warm):
+            fn(i)
+        torch.cuda.synchronize(device)
+        ms_total, _, clocks = timed(fn, steps, world, device, local=local)
+    ms = ms_total / steps
+    peak_gib = reduce_over_ranks(world, torch.cuda.max_memory_allocated(device) / 2**30, device)
+    nv, gemm_f, attn_f = algorithmic_work(cfg, case.lengths)
+    del model, x, m, fn
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    d = {
+        "value": S / (ms / 1e3),
+        "unit": "tokens/s",
+        "ms_per_step": ms,
+        "steps": steps,
+        "n_gpus": world,
+        "parallelism": (f"context parallel x{world}: valid-token balanced chunks, NCCL all-gather of K/V"
+                        if world > 1 else "one GPU"),
+        "chunk_ranges": ranges,
+        "valid_tokens": int(nv),
+        "tflops_valid": (gemm_f + attn_f) / (ms / 1e3) / 1e12,
+        "peak_memory_gib_per_gpu": peak_gib,
+        "clocks": clocks,
+        "gated_by": "tests/test_gpu_layer.py (one GPU) and tests/multi_gpu_worker.py (context parallel): "
+                    "three 256-row query blocks against the query-row oracle",
+    }
+    if headline:
+        d.update({"metric": "layer-forward tokens/s", "warmup": args.warmup,
+                  "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                  "dtype": "fp16 operands, fp32 accumulate/LayerNorm/residual/output",
+                  "data": "synthetic (seeded N(0,1) input, default-init weights, right-padded mask)",
+                  "config": workload_config("long"), "gpu_launches": (2 + 7 * cfg.num_layers) * steps})
+    return d
+
+
+def measure_e2e(case, model, device, args, world, gather, lengths):
     """Same metric through the public API with host buffers: every step copies
-    its input from pinned host memory to the device, runs the forward and
-    copies the output back to pinned host memory, all inside the timed region.
+    its input share from pinned host memory to the device, runs the forward
+    (and, split over N GPUs, the output gather) and copies this rank's share
+    of the output back to pinned host memory, all inside the timed region.
     Steps are pipelined the way a serving loop runs them: the upload of step
     i+1 and the download of step i-1 (two copy streams) overlap the forward of
-    step i (compute stream), with events ordering each step's three stages."""
-    steps = max(3, min(args.steps, 60))  # the pipeline fills and drains once per run
+    step i (compute stream), with events ordering each step's three stages.
+    The pinned-copy bandwidth of rank 0, measured alone, is reported beside
+    it so the host-link limit can be located."""
+    from techjam_b200 import sharding
+
+    steps = max(3, min(args.steps, 60))
     nbuf = 3
+    x_cpu, mask_cpu = case.x_local, case.mask_local
+    # three exchange buffers: the download of step i-3 is the last reader of
+    # the buffer the gather of step i writes, and it completes before step i-1
+    encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches, buffers=3)
+    mine = torch.tensor(case.mine, dtype=torch.int64, device=device)
     x_host = [x_cpu.clone().pin_memory() for _ in range(nbuf)]
     m_host = mask_cpu.pin_memory()
     out_host = [torch.empty_like(x_cpu).pin_memory() for _ in range(nbuf)]
@@ -462,6 +574,13 @@ def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
     fwd_done = [torch.cuda.Event() for _ in range(nbuf)]
     down_done = [torch.cuda.Event() for _ in range(nbuf)]
 
+    def forward(b):
+        if gather:
+            full = encoder.forward(x_dev[b], m_dev[b], gather=True, assignment=case.assignment,
+                                   valid_lengths=lengths)
+            return full.index_select(0, mine)  # this rank's share of the gathered output
+        return model(x_dev[b], m_dev[b])
+
     def run(n):
         for i in range(n + 2):
             if i < n:  # upload step i
@@ -474,8 +593,8 @@ def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
             if 1 <= i <= n:  # forward step i-1
                 b = (i - 1) % nbuf
                 compute.wait_event(up_done[b])
-                compute.wait_event(down_done[b])  # at most nbuf steps in flight
-                outs[b] = model(x_dev[b], m_dev[b])
+                compute.wait_event(down_done[b])  # the download of step i-4 (same host buffer) is done
+                outs[b] = forward(b)
                 fwd_done[b].record(compute)
             if i >= 2:  # download step i-2
                 b = (i - 2) % nbuf
@@ -501,28 +620,50 @@ def measure_e2e(model, x_cpu, mask_cpu, device, args, world):
         compute.wait_stream(h2d)
         end.record(compute)
         torch.cuda.synchronize(device)
-    ms = max_over_ranks(world, start.elapsed_time(end), device) / steps
-    B, S, _ = x_cpu.shape
+        ms = reduce_over_ranks(world, start.elapsed_time(end), device) / steps
+        # pinned copy bandwidth of each rank alone (all ranks at once)
+        bw = {}
+        for name, src, dst in (("h2d", x_host[0], x_dev[0]), ("d2h", x_dev[0], out_host[0])):
+            torch.cuda.synchronize(device)
+            barrier(world, device)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(compute)
+            for _ in range(3):
+                dst.copy_(src, non_blocking=True)
+            e.record(compute)
+            torch.cuda.synchronize(device)
+            bw[name] = 3 * src.numel() * src.element_size() / max(s.elapsed_time(e), 1e-6) / 1e6
+    if gather:
+        encoder.close()
+    B, S = case.cfg_global.batch_size, case.cfg_global.seq_len
+    tokens = B * S * (1 if case.split else world)
     return {
-        "value": B * S * world / (ms / 1e3),
+        "value": tokens / (ms / 1e3),
         "unit": "tokens/s",
         "ms_per_step": ms,
         "steps": steps,
         "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
         "d2h_bytes_per_step": x_cpu.numel() * 4,
+        "bytes_per": "rank (each rank uploads its share and downloads its share of the gathered output)",
+        "pinned_copy_gbs_rank0": {k: round(v, 1) for k, v in bw.items()},
         "pipeline": "upload i+1 / forward i / download i-1 overlapped on 3 streams",
     }
 
 
-def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
-    """Times each kernel alone through its C-ABI entry point on the workload's
+def kernel_breakdown(pkg, model, case, device, args):
+    """Times each kernel alone through its C-ABI entry point on this rank's
     buffers (CUDA events on the launching stream, averaged over repeats)."""
     k = pkg.kernels
+    cfg = case.cfg_local
     B, S, D, H, F = cfg.batch_size, cfg.seq_len, cfg.d_model, cfg.num_heads, cfg.ffn_dim
+    if B == 0:
+        return None
     dh = D // H
     rows = B * S
     layer = model.layers[0]
     att = layer.attention
+    mask = case.mask_local.to(device)
+    x = case.x_local.to(device)
     plan = k.token_plan(mask, B, S, device)
     nv_t, cu, cnt, orig, inv = k.plan_views(plan, B, S)
     nv = int(nv_t.item())
@@ -530,7 +671,6 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
     a16 = torch.empty(rows, D, dtype=torch.float16, device=device)
     qkv = torch.empty(3, H, rows, k.head_pad(dh), dtype=torch.float16, device=device)
     ctx = torch.empty(rows, D, dtype=torch.float16, device=device)
-    x1 = torch.empty(rows, D, dtype=torch.float32, device=device)
     h16 = torch.empty(rows, F, dtype=torch.float16, device=device)
     y16 = torch.empty(rows, D, dtype=torch.float16, device=device)
     y16b = torch.empty(rows, D, dtype=torch.float16, device=device)
@@ -590,7 +730,7 @@ def kernel_breakdown(pkg, model, cfg, x, mask, device, args):
     return res
 
 
-def roofline(kernels, peaks, peak_kind):
+def roofline(kernels, peaks, peak_kind, workload):
     name, k = max(kernels.items(), key=lambda kv: kv[1]["ms"])
     if k["bound"] == "tensor":
         peak = peaks["bf16_tflops"]
@@ -598,7 +738,7 @@ def roofline(kernels, peaks, peak_kind):
     else:
         peak = peaks["hbm_gbs"]
         unit = "GB/s"
-    traffic = load_traffic(name)
+    traffic, source = load_traffic(workload, name)
     return {
         "kernel": name,
         "bound": "tensor" if k["bound"] == "tensor" else "hbm",
@@ -608,104 +748,92 @@ def roofline(kernels, peaks, peak_kind):
         "frac": k["rate"] / peak,
         "peak_source": f"{peak_kind} ({'bf16_tflops burst, kernel timed alone' if unit == 'TFLOP/s' else 'hbm_gbs'})",
         "traffic": traffic,
+        "traffic_source": source,
         "algorithmic_per_launch": k["work"],
     }
 
 
-def load_traffic(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+def load_traffic(workload, kernel):
+    """DRAM bytes per launch of `kernel` on this workload (one GPU's share)
+    from the committed ncu summaries, if any."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
-        return None
+        return None, None
     try:
-        return json.loads(p.read_text()).get(kernel, {}).get("dram_bytes_per_launch")
+        e = json.loads(p.read_text()).get(workload, {}).get(kernel, {})
+        return e.get("dram_bytes_per_launch"), e.get("source")
     except (ValueError, AttributeError):
-        return None
+        return None, None
 
 
 # ---------------------------------------------------------------------------
 # CPU baseline / reference arm (the oracle restatement of the reference's
 # FP32 BaselineTransformer on the host cores)
 # ---------------------------------------------------------------------------
-def cpu_sample(workload, rows):
+def cpu_step_fn(case, sample):
+    """The FP32 oracle forward of one sample of the workload's batch."""
     import oracle
 
-    cfg, sd, x, mask = build_case(workload, 0, torch.device("cpu"))
-    one = oracle.TransformerConfig(rows, *list(cfg.__dict__.values())[1:])
-    xs, ms = x[:rows].contiguous(), mask[:rows].contiguous()
-    if cfg.seq_len > 8192:
-        return lambda: oracle.encoder_forward_blocked(sd, one, xs, ms, query_chunk=1024), one
-    return lambda: oracle.encoder_forward(sd, one, xs, ms), one
+    c = case.cfg_global
+    one = oracle.TransformerConfig(1, c.seq_len, c.d_model, c.num_heads, c.ffn_dim, c.num_layers, c.causal)
+    xs, ms = case.x[sample : sample + 1].contiguous(), case.mask[sample : sample + 1].contiguous()
+    if c.seq_len > 8192:
+        return lambda: oracle.encoder_forward_blocked(case.sd, one, xs, ms, query_chunk=1024)
+    return lambda: oracle.encoder_forward(case.sd, one, xs, ms)
+
+
+def cpu_rotation(workload, steps, budget_s, threads):
+    """Times the oracle on samples 0, 1, 2, ... of the batch in turn (one
+    sample per step, so the steps together cover the batch's length mix),
+    stopping after `steps` steps or the time budget.  Returns (tokens/s on
+    the B*S basis, steps run, seconds, batch size)."""
+    torch.set_num_threads(threads)
+    case = Case(workload, 0, 1)
+    B, S = case.cfg_global.batch_size, case.cfg_global.seq_len
+    cpu_step_fn(case, 0)()  # warm-up (allocator, thread pool)
+    total, n = 0.0, 0
+    t_stop = time.perf_counter() + budget_s
+    while n < steps and (n == 0 or time.perf_counter() < t_stop):
+        fn = cpu_step_fn(case, n % B)
+        t0 = time.perf_counter()
+        fn()
+        total += time.perf_counter() - t0
+        n += 1
+    return n * S / total, n, total, B
 
 
 def cpu_baseline(workload, budget_s=20.0):
     threads = torch.get_num_threads()
-    B, S = WORKLOADS[workload][0], WORKLOADS[workload][1]
-    rows = 1
-    fn, cfg = cpu_sample(workload, rows)
-    t0 = time.perf_counter()
-    fn()
-    one = time.perf_counter() - t0
-    rows = max(1, min(B, int(budget_s / 3 / max(one, 1e-6))))
-    fn, cfg = cpu_sample(workload, rows)
-    fn()
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(times) < 1:
-        t0 = time.perf_counter()
-        fn()
-        times.append(time.perf_counter() - t0)
-        if len(times) >= 5:
-            break
-    med = statistics.median(times)
-    return {
-        "value": rows * S / med,
-        "unit": "tokens/s",
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{rows} of {B} sequences of the same batch (S={S}), FP32 oracle, median of {len(times)} runs",
-    }
+    value, n, total, B = cpu_rotation(workload, 10**6, budget_s, threads)
+    return {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"samples 0..{n - 1} of the {B}-sequence batch, one per step (the FP32 oracle "
+                      f"restatement of BaselineTransformer, {total:.1f} s)"}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    B, S = WORKLOADS[args.workload][0], WORKLOADS[args.workload][1]
-    fn, cfg = cpu_sample(args.workload, 1)
-    for _ in range(max(1, min(args.warmup, 2))):
-        fn()
-    budget = args.cpu_budget * 6
-    times = []
-    t_stop = time.perf_counter() + budget
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        fn()
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_stop:
-            break
-    total = sum(times)
-    value = len(times) * S / total
+    value, n, total, B = cpu_rotation(args.workload, args.steps, args.cpu_budget * 6, threads)
     return {
         "metric": "layer-forward tokens/s",
         "value": value,
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": len(times),
+        "steps": n,
         "steps_requested": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": total / len(times) * 1e3,
+        "ms_per_step": total / n * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload in SPLIT_BATCH else "weak",
         "vs_baseline": None,
         "dtype": "fp32",
         "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
-        "config": {"workload": WORKLOADS[args.workload][-1], "global_batch": B, "seq_len": S},
+        "config": workload_config(args.workload),
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"one sequence (S={S}) of the batch per step, FP32 oracle restatement "
-                                   "of BaselineTransformer"},
+                         "sample": f"samples 0..{n - 1} of the {B}-sequence batch, one per step (the FP32 oracle "
+                                   "restatement of BaselineTransformer on all host threads)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -732,7 +860,7 @@ def attention_length_scan(args):
         cnt = torch.full((B, 1), L, dtype=torch.int32, device=device)
         qkv = torch.randn(3, H, rows, dh, device=device, generator=g).half()
         ctx = torch.empty(rows, H * dh, dtype=torch.float16, device=device)
-        fn = lambda: k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, cu[:-1].contiguous().view(-1, 1), cnt, L,
+        fn = lambda: k.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, cu[:-1].contiguous().view(-1, 1), cnt, L,  # noqa: E731
                                       dh ** -0.5, out=ctx)
         for _ in range(args.warmup):
             fn()
@@ -759,12 +887,16 @@ def attention_length_scan(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="dense")
+    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="batch")
+    ap.add_argument("--micro-batches", type=int, default=2,
+                    help="micro-batches per rank in the split-batch gather (overlap of the gather)")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="headline only (no nested dense / context-parallel / sustained measurements)")
     ap.add_argument("--attention-scan", action="store_true",
                     help="time the attention kernel alone over sequence lengths 256..65536 instead")
     args = ap.parse_args()
