@@ -297,7 +297,9 @@ TJ_API int tj_copy_segments(const tj_copy_segment* segs, int n, void* stream);
  *     TJ_NOALLOC_WORKSPACE_BYTES are rejected with TJ_ERR_WORKSPACE.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The address is cached per device and CUDA
+ *     context: after a device reset, or from another context on the device,
+ *     the next call looks it up again (make that call outside capture too).
  *   - All calls share the one array: calls that overlap on the GPU (other
  *     streams or threads) race.  Nothing in it needs to start at zero. */
 TJ_API int tj_encoder_forward_noalloc(const tj_encoder_desc* desc, const tj_layer_weights* layers,

@@ -11,8 +11,10 @@
 // The array is a file-scope __device__ variable, so every GPU that loads this
 // library holds TJ_NOALLOC_WORKSPACE_BYTES of it until the process exits.  In
 // host code its name is only a host-side stand-in, never a device address: the
-// real address comes from cudaGetSymbolAddress, looked up once per device on
-// the first call made with that device current, and cached.
+// real address comes from cudaGetSymbolAddress, looked up on the first call
+// made with a device current and cached for that device and its current CUDA
+// context (a device reset or another context on the device makes the next
+// call look it up again).
 #include <mutex>
 
 #include "common.cuh"
@@ -22,8 +24,25 @@ namespace tj {
 
 static __device__ __align__(256) uint8_t g_noalloc_workspace[TJ_NOALLOC_WORKSPACE_BYTES];
 
+typedef CUresult (*PfnCtxGetCurrent)(CUcontext*);
+
 static std::mutex g_noalloc_mu;
 static void* g_noalloc_ptr[64] = {nullptr};
+static CUcontext g_noalloc_ctx[64] = {nullptr};
+
+static PfnCtxGetCurrent ctx_get_current_fn() {
+  static PfnCtxGetCurrent fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfnCtxGetCurrent>(ptr);
+    tried = true;
+  }
+  return fn;
+}
 
 // Device address of g_noalloc_workspace on the current device.
 static int noalloc_workspace(void** out) {
@@ -31,14 +50,21 @@ static int noalloc_workspace(void** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return set_error(TJ_ERR_UNSUPPORTED, "device index %d", dev);
+  // The context current on this thread (null before the runtime has made one
+  // current here; the lookup below does that, and the next call then sees
+  // the real context and looks the address up once more).
+  CUcontext ctx = nullptr;
+  PfnCtxGetCurrent get_ctx = ctx_get_current_fn();
+  if (get_ctx) get_ctx(&ctx);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_workspace);
     if (e != cudaSuccess || p == nullptr)
       return set_error(TJ_ERR_CUDA, "encoder_forward_noalloc: cudaGetSymbolAddress failed: %s",
                        cudaGetErrorString(e));
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return TJ_OK;

@@ -346,6 +346,12 @@ class ContextParallelEncoder:
         if Sl > slab:
             raise ValueError(f"local chunk {Sl} longer than slab {slab}")
         H, F = cfg.num_heads, cfg.ffn_dim
+        if D % 8 or F % 8:
+            # The per-kernel entry points take dense fp16 rows, which TMA needs
+            # to be whole 16-byte units; the single-GPU encoder pads its own
+            # buffers instead (tj_encoder_forward).
+            raise ValueError(f"context parallelism needs d_model and ffn_dim that are multiples of 8 "
+                             f"(got {D} and {F}); run such a model on one GPU")
         dh = D // H
         x = x_local.contiguous().view(Sl, D)
         if mask_local is not None:

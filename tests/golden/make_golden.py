@@ -3,7 +3,7 @@
 Run in a container that has the reference repository checked out (read-only
 is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 It imports the reference's own FP32 model, input generator and memory-bounded
 oracle (torch_transformer_benchmark.py, tools/shape14/accuracy.py), runs them
@@ -51,7 +51,7 @@ def row_stats(out: torch.Tensor):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference repository checkout")
     args = ap.parse_args()
     ref_root = Path(args.reference)
     sys.path.insert(0, str(ref_root))

@@ -360,12 +360,16 @@ def test_flash_attention_rising_max(cuda_pkg, pattern, causal):
 
 
 def test_flash_attention_more_samples_than_grid_rows(cuda_pkg):
-    """70000 samples (of 1-3 tokens): more than the 65535 rows of one launch's
-    grid, so the library runs it as two launches."""
+    """70000 samples (of 1-3 tokens, and four of 200 tokens placed after grid
+    row 65535): more than the 65535 rows of one launch's grid, so the library
+    runs it as two launches; the long samples check that the second launch
+    finds its samples through its first-row offset."""
     k = cuda_pkg.kernels
     g = torch.Generator().manual_seed(70000)
     B, H = 70000, 1
     lens = torch.randint(1, 4, (B,), generator=g, dtype=torch.int32)
+    long_ids = (65535, 65540, 68000, 69999)
+    lens[list(long_ids)] = 200
     cu = torch.zeros(B + 1, dtype=torch.int32)
     cu[1:] = torch.cumsum(lens, 0)
     rows = int(cu[-1])
@@ -373,11 +377,11 @@ def test_flash_attention_more_samples_than_grid_rows(cuda_pkg):
     scale = 64**-0.5
     dev = qkv.to(DEV)
     out = k.flash_attn_fwd(dev[0], dev[1:2], dev[2:3], cu.to(DEV), cu[:-1].view(-1, 1).contiguous().to(DEV),
-                           lens.view(-1, 1).contiguous().to(DEV), 3, scale).float().cpu()
+                           lens.view(-1, 1).contiguous().to(DEV), 200, scale).float().cpu()
     # Reference per length group (every sample of length L at once).
     ref = torch.zeros(rows, H * 64)
     q, kk, vv = qkv[0, 0].float(), qkv[1, 0].float(), qkv[2, 0].float()
-    for L in (1, 2, 3):
+    for L in (1, 2, 3, 200):
         idx = torch.nonzero(lens == L).flatten()
         rws = (cu[idx].long()[:, None] + torch.arange(L)[None, :])  # [n, L]
         s = torch.einsum("nid,njd->nij", q[rws], kk[rws]) * scale

@@ -62,6 +62,51 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_pkg):
         assert torch.count_nonzero(out.cpu()[~mask]) == 0
 
 
+def _near_bound_seq_len(cuda_pkg, lib, B, D, H, F, L):
+    """Largest S (multiple of 64) whose workspace still fits the static array."""
+    S = 64
+    while True:
+        desc = cuda_pkg._lib.EncoderDesc(B, S + 64, D, H, F, L, 0, 1e-5)
+        if lib.tj_encoder_workspace_bytes(ctypes.byref(desc)) > (64 << 20):
+            return S
+        S += 64
+
+
+@pytest.mark.parametrize("case", ["two_layers_causal", "near_the_bound"])
+def test_noalloc_multi_layer_and_near_the_bound(cuda_pkg, case):
+    """Every workspace buffer in use (two layers: x1, x2 and the last layer's
+    FFN-out all live in the static array), and a shape whose workspace fills
+    the array to within one 64-token step, where a layout error would first
+    show: two calls in a row, each against tj_encoder_forward."""
+    lib = cuda_pkg._lib.load()
+    if case == "two_layers_causal":
+        t = (2, 320, 256, 4, 1024, 2, True)
+    else:
+        t = (4, _near_bound_seq_len(cuda_pkg, lib, 4, 256, 4, 1024, 2), 256, 4, 1024, 2, False)
+    cfg = oracle.TransformerConfig(*t)
+    desc = cuda_pkg._lib.EncoderDesc(*t[:6], 1 if t[6] else 0, 1e-5)
+    need = lib.tj_encoder_workspace_bytes(ctypes.byref(desc))
+    assert 0 < need <= (64 << 20)
+    if case == "near_the_bound":
+        assert need > (64 << 20) - 4 * 64 * 8192  # within one 64-token step of the limit
+    sd = oracle.make_state_dict(cfg, seed=77)
+    model = cuda_pkg.UserOptimizedTransformer(cuda_pkg.TransformerConfig(*t))
+    model.load_state_dict(sd, strict=True)
+    model = model.to(DEV).eval()
+    for seed, pad in ((77, 0.3), (78, 0.7)):
+        x, mask = oracle.generate_random_case(cfg, seed=seed, padding_ratio=pad)
+        xd, md = x.to(DEV).contiguous(), mask.to(DEV).contiguous()
+        with torch.inference_mode():
+            expected = model(xd, md)
+        out = torch.full_like(xd, float("nan"))
+        rc = _noalloc(lib, model, desc, xd, md, out)
+        assert rc == 0, cuda_pkg._lib.last_error()
+        torch.cuda.synchronize()
+        r = oracle.compare_outputs(expected.cpu(), out.cpu(), rtol=0.02, atol=0.002)
+        assert r.passed, (case, seed, r)
+        assert torch.count_nonzero(out.cpu()[~mask]) == 0
+
+
 def test_noalloc_rejects_shapes_beyond_the_static_workspace(cuda_pkg):
     lib = cuda_pkg._lib.load()
     desc = cuda_pkg._lib.EncoderDesc(8, 2048, 1024, 16, 4096, 1, 0, 1e-5)
