@@ -15,8 +15,10 @@
  * exception crosses this boundary.
  *
  * Device-side failures (a pipeline wait inside a kernel that exceeded its time
- * limit) are recorded in a per-device status word instead of hanging or
- * trapping the GPU; tj_device_status() reads and clears it.  With
+ * limit, code 1; a row table in device memory that points outside its
+ * buffer, code 2) are recorded in a per-device status word instead of
+ * hanging, trapping or faulting the GPU; tj_device_status() reads and clears
+ * it.  With
  * tj_set_sync_check(1) every entry point synchronises its stream and reports a
  * recorded device error as TJ_ERR_DEVICE (debugging and tests only).
  *
@@ -77,6 +79,23 @@ TJ_API int tj_set_sync_check(int enabled);
  * and clears it.  Returns TJ_OK, or TJ_ERR_DEVICE if a device error was
  * recorded, or TJ_ERR_CUDA if the synchronise itself failed. */
 TJ_API int tj_device_status(int* out4, void* stream);
+
+/* ---- debugging and tests (no reference counterpart) ---------------------
+ * Device-side failure detection is tested without a GPU fault: a test
+ * shortens the wait limit and withholds one barrier arrive, the wait runs
+ * out, the kernel records the site and returns, and tj_device_status reports
+ * it.  Both settings are per device (the current one) and stay until reset. */
+
+/* Time limit of every pipeline wait inside the kernels, in nanoseconds
+ * (0 restores the default, 2 s). */
+TJ_API int tj_debug_set_wait_limit_ns(uint64_t ns);
+
+#define TJ_WITHHOLD_NONE 0
+#define TJ_WITHHOLD_ATTN_P_READY 1 /* attention: the first "P ready" arrive of each CTA (wait site 213) */
+
+/* Makes every following kernel launch on the current device withhold the
+ * selected barrier arrive (TJ_WITHHOLD_NONE to stop).  Tests only. */
+TJ_API int tj_debug_withhold_arrive(int which);
 
 /* ---- token plan --------------------------------------------------------- */
 

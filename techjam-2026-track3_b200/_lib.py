@@ -20,6 +20,9 @@ TJ_ERR_CUDA = 3
 TJ_ERR_DEVICE = 4
 TJ_ERR_WORKSPACE = 5
 
+TJ_WITHHOLD_NONE = 0
+TJ_WITHHOLD_ATTN_P_READY = 1
+
 _ERR_NAMES = {
     TJ_ERR_INVALID_ARGUMENT: "invalid argument",
     TJ_ERR_UNSUPPORTED: "unsupported",
@@ -78,6 +81,8 @@ SIGNATURES = {
     "tj_get_last_error": (c_int, [ctypes.c_char_p, ctypes.c_size_t]),
     "tj_set_sync_check": (c_int, [c_int]),
     "tj_device_status": (c_int, [ctypes.POINTER(c_int), c_vp]),
+    "tj_debug_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
+    "tj_debug_withhold_arrive": (c_int, [c_int]),
     "tj_token_plan_ints": (c_i64, [c_int, c_int]),
     "tj_token_plan": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     "tj_ln_cast_f16": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),

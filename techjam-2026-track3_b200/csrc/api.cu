@@ -18,6 +18,8 @@
 
 namespace tj {
 
+static_assert(kWithholdAttnPFull == TJ_WITHHOLD_ATTN_P_READY, "withhold switch numbering");
+
 static thread_local std::string g_last_error;
 static std::atomic<int> g_sync_check{0};
 
@@ -130,11 +132,31 @@ int tj_device_status(int* out4, void* stream) {
   if (host[0] != 0) {
     const int zero[4] = {0, 0, 0, 0};
     cudaMemcpyToSymbol(g_status, zero, sizeof(zero));
-    return set_error(TJ_ERR_DEVICE,
-                     "device error %d recorded by a kernel (wait site %d, block %d,%d): a pipeline "
-                     "wait exceeded its time limit",
-                     host[0], host[1], host[2], host[3]);
+    return set_error(TJ_ERR_DEVICE, "device error %d recorded by a kernel (site %d, block %d,%d): %s", host[0],
+                     host[1], host[2], host[3],
+                     host[0] == kDevWaitTimeout   ? "a pipeline wait exceeded its time limit"
+                     : host[0] == kDevBadArgument ? "a row table in device memory points outside its buffer"
+                                                  : "unknown code");
   }
+  return TJ_OK;
+}
+
+int tj_debug_set_wait_limit_ns(uint64_t ns) {
+  int rc = check_device();
+  if (rc) return rc;
+  const unsigned long long v = ns ? (unsigned long long)ns : kWaitLimitNs;
+  cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v));
+  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "debug_set_wait_limit_ns: %s", cudaGetErrorString(e));
+  return TJ_OK;
+}
+
+int tj_debug_withhold_arrive(int which) {
+  int rc = check_device();
+  if (rc) return rc;
+  if (which != 0 && which != kWithholdAttnPFull)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "debug_withhold_arrive: unknown switch %d", which);
+  cudaError_t e = cudaMemcpyToSymbol(g_debug_withhold, &which, sizeof(which));
+  if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "debug_withhold_arrive: %s", cudaGetErrorString(e));
   return TJ_OK;
 }
 

@@ -104,7 +104,28 @@ struct AttnKernelParams {
   int dh_out;  // real head dim (<= DH): columns of ctx written per head
   const int32_t* order;  // optional: sample handled by grid row z (longest first)
   int z0;                // first grid row of this launch (batches above 65535 take several)
+  int q_rows, kv_rows;   // rows of the Q slab and of one K/V slab (bounds of the row tables)
 };
+
+// The row tables (q_cu, kv_off, kv_len, order) live in device memory, written
+// by the caller or an earlier kernel, so the host cannot check them without a
+// synchronise.  Every CTA checks the entries it uses before any load or store:
+// an out-of-range entry is recorded as kDevBadArgument (wait site 230) in the
+// status word and the CTA returns without touching memory.
+__device__ __forceinline__ bool attn_tables_ok(const AttnKernelParams& p, int zb, int* b_out) {
+  const int b = p.order ? p.order[zb] : zb;
+  if (b < 0 || b >= p.B) return false;
+  const int q0 = p.q_cu[b], q1 = p.q_cu[b + 1];
+  if (q0 < 0 || q1 < q0 || q1 > p.q_rows) return false;
+  const int32_t* off = p.kv_off + (int64_t)b * p.kv_len_stride;
+  const int32_t* len = p.kv_len + (int64_t)b * p.kv_len_stride;
+  for (int g = 0; g < p.G; ++g) {
+    const int n = len[g];
+    if (n > 0 && (off[g] < 0 || (int64_t)off[g] + n > p.kv_rows)) return false;
+  }
+  *b_out = b;
+  return true;
+}
 
 // Walks the key tiles of one sample in order: segment g, tile i inside it.
 // Every role walks the same sequence, so tile j means the same keys to each.
@@ -175,7 +196,11 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
   const int h = blockIdx.y;
   pdl_wait();  // q/k/v and the token plan come from earlier kernels
   const int zb = p.z0 + (int)blockIdx.z;
-  const int b = p.order ? p.order[zb] : zb;
+  int b = 0;
+  if (!attn_tables_ok(p, zb, &b)) {  // uniform for the CTA
+    if (threadIdx.x == 0) report_error(kDevBadArgument, 230);
+    return;
+  }
   const int q_begin = p.q_cu[b];
   const int nq = p.q_cu[b + 1] - q_begin;
   const int q_tile0 = blockIdx.x * NT;
@@ -438,6 +463,8 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
       float m_run = -INFINITY;  // running max (log2 units, stale by at most 8)
       float l_run = 0.f;
       bool ok = true;
+      // test-only: the first warpgroup withholds its first "P ready" arrive
+      const bool withhold = t == 0 && *((volatile int*)&g_debug_withhold) == kWithholdAttnPFull;
 
       KvWalk w;
       w.init(kv_off, kv_len, p.G, BN);
@@ -553,7 +580,7 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
         l_run += a.x + a.y;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full(t));
+        if (lane == 0 && !(withhold && j == 0)) mbar_arrive(p_full(t));
       }
       if (ok && T > 0) {
         ok = mbar_wait(pv_done(t), (uint32_t)((T - 1) & 1), abort_flag, 222);
@@ -668,6 +695,8 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   kp.ld_ctx = a.ld_ctx ? (int)a.ld_ctx : a.H * a.head_dim;
   kp.dh_out = a.head_dim;
   kp.order = a.order;
+  kp.q_rows = a.q_rows;
+  kp.kv_rows = a.kv_rows;
   constexpr int kQPerCta = Cfg::NT * kAttnBM;
   if (a.H > 65535) return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d above 65535", a.H);
   // Grid rows are samples; a batch above the 65535-row limit runs as several

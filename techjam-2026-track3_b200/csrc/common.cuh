@@ -4,7 +4,7 @@
 // reports into.
 //
 // Every wait on an mbarrier goes through `mbar_wait`, which gives up after
-// kWaitLimitNs of wall time, records the wait site in the device status word
+// g_wait_limit_ns (2 s) of wall time, records the wait site in the device status word
 // and sets the CTA-wide abort flag.  The other warps of the CTA see the abort
 // flag on their next wait and leave their loops, so the kernel always returns
 // and the host reads a non-zero status instead of a hung GPU.
@@ -32,6 +32,19 @@ enum DeviceError : int {
 __device__ int g_status[4];
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+// Pipeline waits give up after g_wait_limit_ns (kWaitLimitNs unless a test
+// shortened it with tj_debug_set_wait_limit_ns).  The drain waits at the end
+// of a kernel (letting its own copies and MMAs finish before it exits) keep
+// kWaitLimitNs.
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+
+// Test-only fault injection on the host's request (tj_debug_withhold_arrive):
+// when set to kWithholdAttnPFull, every attention CTA's first softmax warpgroup
+// skips its first "P ready" arrive, so the MMA warp's wait on it (site 213)
+// runs out; no TMA transfer depends on that arrive.  0 in normal operation.
+__device__ int g_debug_withhold;
+constexpr int kWithholdAttnPFull = 1;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -146,13 +159,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           int site) {
   if (mbar_try_wait<kCluster>(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
+  const unsigned long long limit = *((volatile unsigned long long*)&g_wait_limit_ns);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i) {
       if (mbar_try_wait<kCluster>(bar, parity)) return true;
     }
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       report_error(kDevWaitTimeout, site);
       *abort_flag = 1;
       return false;
