@@ -222,6 +222,28 @@ TJ_API int tj_flash_attn_fwd_strided(const void* q16, const void* k16, const voi
                               float scale, int causal, const int32_t* q_pos0, void* ctx16,
                               int64_t ld_ctx, void* stream);
 
+/* tj_flash_attn_fwd_strided over part of each sample's keys, for attention
+ * split into two launches (context parallelism: a rank's own keys while the
+ * other ranks' keys are still arriving, then those).  part_mode:
+ *   1  writes the partial result of these keys instead of ctx16 (which may be
+ *      NULL): part_o [q_rows][num_heads*head_dim] fp32, the normalised context
+ *      of these keys, and part_lse [q_rows][num_heads], log2 of their softmax
+ *      denominator in base-2 units (log2 of the sum of 2^(s*scale*log2 e) over
+ *      the keys; -inf for a row without keys);
+ *   2  merges these keys' result with that partial and writes ctx16, equal to
+ *      attention over both key sets in one launch up to rounding;
+ *   0  plain tj_flash_attn_fwd_strided.
+ * part_o must be 16-byte aligned.  A query row's two launches must use the
+ * same q rows, scale and head layout.  Replaces, with the key set split, the
+ * SDPA call of v16_1_clean.py:505-514. */
+TJ_API int tj_flash_attn_fwd_partial(const void* q16, const void* k16, const void* v16, int num_heads,
+                              int head_dim, int q_rows, int kv_rows, int64_t kv_stride_h,
+                              int64_t kv_stride_g, int num_segments, int batch, int max_q_per_sample,
+                              const int32_t* q_cu, const int32_t* kv_off, const int32_t* kv_len,
+                              float scale, int causal, const int32_t* q_pos0, void* ctx16,
+                              int64_t ld_ctx, float* part_o, float* part_lse, int part_mode,
+                              void* stream);
+
 /* ---- whole encoder ----------------------------------------------------- */
 
 typedef struct tj_encoder_desc {

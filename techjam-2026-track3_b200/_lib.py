@@ -120,6 +120,13 @@ SIGNATURES = {
             c_vp, c_vp, c_vp, c_float, c_int, c_vp, c_vp, c_i64, c_vp,
         ],
     ),
+    "tj_flash_attn_fwd_partial": (
+        c_int,
+        [
+            c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_i64, c_int, c_int, c_int,
+            c_vp, c_vp, c_vp, c_float, c_int, c_vp, c_vp, c_i64, c_vp, c_vp, c_int, c_vp,
+        ],
+    ),
     "tj_encoder_workspace_bytes": (c_i64, [ctypes.POINTER(EncoderDesc)]),
     "tj_encoder_forward": (
         c_int,

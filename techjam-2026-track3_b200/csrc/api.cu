@@ -309,12 +309,13 @@ int tj_gemm_bias_gelu_f16(const void* a16, const void* w16, const float* bias,
   return finish(launch_gemm(kEpiGeluF16, a, s), s);
 }
 
-int tj_flash_attn_fwd_strided(const void* q16, const void* k16, const void* v16, int num_heads,
+int tj_flash_attn_fwd_partial(const void* q16, const void* k16, const void* v16, int num_heads,
                               int head_dim, int q_rows, int kv_rows, int64_t kv_stride_h,
                               int64_t kv_stride_g, int num_segments, int batch, int max_q_per_sample,
                               const int32_t* q_cu, const int32_t* kv_off, const int32_t* kv_len,
                               float scale, int causal, const int32_t* q_pos0, void* ctx16,
-                              int64_t ld_ctx, void* stream) {
+                              int64_t ld_ctx, float* part_o, float* part_lse, int part_mode,
+                              void* stream) {
   int rc = check_device();
   if (rc) return rc;
   AttnArgs a{};
@@ -339,8 +340,23 @@ int tj_flash_attn_fwd_strided(const void* q16, const void* k16, const void* v16,
   a.q_pos0 = q_pos0;
   a.ctx = ctx16;
   a.ld_ctx = ld_ctx;
+  a.part_o = part_o;
+  a.part_lse = part_lse;
+  a.part_mode = part_mode;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return finish(launch_attention(a, s), s);
+}
+
+int tj_flash_attn_fwd_strided(const void* q16, const void* k16, const void* v16, int num_heads,
+                              int head_dim, int q_rows, int kv_rows, int64_t kv_stride_h,
+                              int64_t kv_stride_g, int num_segments, int batch, int max_q_per_sample,
+                              const int32_t* q_cu, const int32_t* kv_off, const int32_t* kv_len,
+                              float scale, int causal, const int32_t* q_pos0, void* ctx16,
+                              int64_t ld_ctx, void* stream) {
+  return tj_flash_attn_fwd_partial(q16, k16, v16, num_heads, head_dim, q_rows, kv_rows, kv_stride_h,
+                                   kv_stride_g, num_segments, batch, max_q_per_sample, q_cu, kv_off,
+                                   kv_len, scale, causal, q_pos0, ctx16, ld_ctx, nullptr, nullptr, 0,
+                                   stream);
 }
 
 int tj_flash_attn_fwd(const void* q16, const void* k16, const void* v16, int num_heads,

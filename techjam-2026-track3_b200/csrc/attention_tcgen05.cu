@@ -105,6 +105,16 @@ struct AttnKernelParams {
   const int32_t* order;  // optional: sample handled by grid row z (longest first)
   int z0;                // first grid row of this launch (batches above 65535 take several)
   int q_rows, kv_rows;   // rows of the Q slab and of one K/V slab (bounds of the row tables)
+  // Split attention over two launches (context parallelism: the rank's own
+  // keys first, the other ranks' keys once they have arrived).  part_mode 1
+  // writes this launch's partial result instead of ctx: the normalised fp32
+  // context part_o [q_rows][H*dh_out] and part_lse [q_rows][H] = log2 of the
+  // softmax denominator in base-2 units (log2 sum 2^(s*scale*log2e)), -inf
+  // for a row without keys.  part_mode 2 merges its own keys' result with
+  // that partial and writes ctx.  part_mode 0: ctx only.
+  float* part_o;
+  float* part_lse;
+  int part_mode;
 };
 
 // The row tables (q_cu, kv_off, kv_len, order) live in device memory, written
@@ -588,8 +598,33 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
       }
       ok = __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
       if (ok) {  // warp-uniform: the TMEM loads below are warp-collective
-        const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-        __half* dst = p.ctx + (int64_t)(q_begin + q_local) * p.ld_ctx + h * p.dh_out;
+        // out = O * f_o + prior * f_p, prior = the partial result of an
+        // earlier launch over other keys (part_mode 2).  O and l_run are
+        // relative to 2^m_run, so this launch's log2-sum-exp is
+        // m_run + log2(l_run) (-inf without keys).
+        const bool row_ok = q_local < nq;
+        const int64_t row = (int64_t)q_begin + q_local;
+        const float e_cur = l_run > 0.f ? m_run : -INFINITY;
+        float f_o = l_run > 0.f ? 1.0f / l_run : 0.f, f_p = 0.f;
+        if (p.part_mode == 2 && row_ok) {
+          const float lse_p = p.part_lse[row * p.H + h];
+          const float mx = fmaxf(e_cur, lse_p);
+          if (mx == -INFINITY) {
+            f_o = 0.f;
+          } else {
+            const float a = e_cur == -INFINITY ? 0.f : exp2_approx(e_cur - mx);
+            const float b2 = lse_p == -INFINITY ? 0.f : exp2_approx(lse_p - mx);
+            const float inv = 1.0f / (l_run * a + b2);
+            f_o = a * inv;
+            f_p = b2 * inv;
+          }
+        }
+        if (p.part_mode == 1 && row_ok)
+          p.part_lse[row * p.H + h] = l_run > 0.f ? e_cur + __log2f(l_run) : -INFINITY;
+        const int ld_part = p.H * p.dh_out;
+        float* prow = p.part_mode ? p.part_o + row * ld_part + h * p.dh_out : nullptr;
+        const bool vec_part = (p.dh_out & 3) == 0;
+        __half* dst = p.part_mode == 1 ? nullptr : p.ctx + row * p.ld_ctx + h * p.dh_out;
 #pragma unroll 1
         for (int c = 0; c < DH / 32; ++c) {
           if (32 * c >= p.dh_out) break;
@@ -601,15 +636,48 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
 #pragma unroll
             for (int d = 0; d < 32; ++d) o[d] = 0u;
           }
-          if (q_local >= nq) continue;
-          if ((p.dh_out & 7) == 0 && 32 * c + 32 <= p.dh_out) {
+          if (!row_ok) continue;
+          const bool full = 32 * c + 32 <= p.dh_out;
+          float val[32];
+#pragma unroll
+          for (int d = 0; d < 32; ++d) val[d] = __uint_as_float(o[d]) * f_o;
+          if (p.part_mode == 1) {
+            if (vec_part && full) {
+#pragma unroll
+              for (int g = 0; g < 8; ++g)
+                reinterpret_cast<float4*>(prow + 32 * c)[g] =
+                    make_float4(val[4 * g], val[4 * g + 1], val[4 * g + 2], val[4 * g + 3]);
+            } else {
+#pragma unroll
+              for (int d = 0; d < 32; ++d)
+                if (32 * c + d < p.dh_out) prow[32 * c + d] = val[d];
+            }
+            continue;
+          }
+          if (p.part_mode == 2) {
+            if (vec_part && full) {
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const float4 q4 = reinterpret_cast<const float4*>(prow + 32 * c)[g];
+                val[4 * g] += q4.x * f_p;
+                val[4 * g + 1] += q4.y * f_p;
+                val[4 * g + 2] += q4.z * f_p;
+                val[4 * g + 3] += q4.w * f_p;
+              }
+            } else {
+#pragma unroll
+              for (int d = 0; d < 32; ++d)
+                if (32 * c + d < p.dh_out) val[d] += prow[32 * c + d] * f_p;
+            }
+          }
+          if ((p.dh_out & 7) == 0 && full) {
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
               uint4 v;
-              v.x = pack_half2(__uint_as_float(o[8 * g + 0]) * inv_l, __uint_as_float(o[8 * g + 1]) * inv_l);
-              v.y = pack_half2(__uint_as_float(o[8 * g + 2]) * inv_l, __uint_as_float(o[8 * g + 3]) * inv_l);
-              v.z = pack_half2(__uint_as_float(o[8 * g + 4]) * inv_l, __uint_as_float(o[8 * g + 5]) * inv_l);
-              v.w = pack_half2(__uint_as_float(o[8 * g + 6]) * inv_l, __uint_as_float(o[8 * g + 7]) * inv_l);
+              v.x = pack_half2(val[8 * g + 0], val[8 * g + 1]);
+              v.y = pack_half2(val[8 * g + 2], val[8 * g + 3]);
+              v.z = pack_half2(val[8 * g + 4], val[8 * g + 5]);
+              v.w = pack_half2(val[8 * g + 6], val[8 * g + 7]);
               reinterpret_cast<uint4*>(dst + 32 * c)[g] = v;
             }
           } else {
@@ -617,7 +685,7 @@ __global__ void __launch_bounds__(AttnCfg<DH, SHORT>::kThreads, AttnCfg<DH, SHOR
             // columns are dropped.
 #pragma unroll
             for (int d = 0; d < 32; ++d)
-              if (32 * c + d < p.dh_out) dst[32 * c + d] = __float2half_rn(__uint_as_float(o[d]) * inv_l);
+              if (32 * c + d < p.dh_out) dst[32 * c + d] = __float2half_rn(val[d]);
           }
         }
       }
@@ -697,6 +765,9 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   kp.order = a.order;
   kp.q_rows = a.q_rows;
   kp.kv_rows = a.kv_rows;
+  kp.part_o = a.part_o;
+  kp.part_lse = a.part_lse;
+  kp.part_mode = a.part_mode;
   constexpr int kQPerCta = Cfg::NT * kAttnBM;
   if (a.H > 65535) return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: H=%d above 65535", a.H);
   // Grid rows are samples; a batch above the 65535-row limit runs as several
@@ -717,10 +788,14 @@ int launch_attention(const AttnArgs& a, cudaStream_t stream) {
     return set_error(TJ_ERR_UNSUPPORTED, "flash_attn_fwd: head_dim %d (1..256 supported)", a.head_dim);
   if (a.H <= 0 || a.B <= 0 || a.G <= 0 || a.q_rows < 0 || a.kv_rows < 0 || a.max_q_per_sample < 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: bad sizes H=%d B=%d G=%d", a.H, a.B, a.G);
-  if (!a.q || !a.k || !a.v || !a.ctx || !a.q_cu || !a.kv_off || !a.kv_len)
+  if (a.part_mode < 0 || a.part_mode > 2)
+    return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: part_mode %d (0, 1 or 2)", a.part_mode);
+  if (!a.q || !a.k || !a.v || (a.part_mode != 1 && !a.ctx) || !a.q_cu || !a.kv_off || !a.kv_len ||
+      (a.part_mode != 0 && (!a.part_o || !a.part_lse)))
     return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: null pointer");
   if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
-       reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.ctx)) & 15u)
+       reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.ctx) |
+       reinterpret_cast<uintptr_t>(a.part_o)) & 15u)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: operands must be 16-byte aligned");
   if (a.kv_stride_h % 8 != 0 || a.kv_stride_g % 8 != 0)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "flash_attn_fwd: K/V strides must be multiples of 8 elements");

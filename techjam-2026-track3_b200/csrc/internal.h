@@ -127,6 +127,9 @@ struct AttnArgs {
   const int32_t* order;     // optional [B]: sample of each grid row (longest first)
   void* ctx;                // fp16 [q_rows][ld_ctx]: head h in columns [h*dh, h*dh + dh)
   int64_t ld_ctx;           // elements between context rows; 0 = H*dh
+  float* part_o;            // partial context fp32 [q_rows][H*dh] (part_mode 1 writes, 2 reads)
+  float* part_lse;          // partial log2-sum-exp [q_rows][H]
+  int part_mode;            // 0 ctx, 1 write the partial, 2 merge with the partial into ctx
 };
 
 int launch_attention(const AttnArgs& args, cudaStream_t stream);

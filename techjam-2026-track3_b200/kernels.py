@@ -295,11 +295,16 @@ def gemm_bias_gelu_f16(a16, w16, bias, row_count=None, out=None):
 
 
 def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causal=False,
-                   q_pos0=None, out=None, head_dim=64):
+                   q_pos0=None, out=None, head_dim=64, part_o=None, part_lse=None, part_mode=0):
     """q: [H, q_rows, P]; k, v: [G, H, kv_rows, P] with P = head_pad(head_dim) (any strides
     with unit inner stride; rows hold head_dim values then zeros up to P); q_cu: [B+1];
     kv_off/kv_len: [B, G]
-    int32.  Returns ctx [q_rows, H*head_dim] fp16."""
+    int32.  Returns ctx [q_rows, H*head_dim] fp16.
+
+    Split attention (tj_flash_attn_fwd_partial): part_mode 1 writes the partial
+    result of these keys into part_o [q_rows, H*head_dim] fp32 and part_lse
+    [q_rows, H] fp32 and returns None; part_mode 2 merges these keys with that
+    partial into ctx."""
     dev = q.device
     _require(q, "q", torch.float16, dev)
     if k.dim() == 3:
@@ -313,25 +318,33 @@ def flash_attn_fwd(q, k, v, q_cu, kv_off, kv_len, max_q_per_sample, scale, causa
     if k.stride() != v.stride() or k.stride(-1) != 1 or k.stride(-2) != P:
         raise ValueError(f"k and v must share strides with contiguous [rows, {P}] slabs")
     B = q_cu.numel() - 1
-    if out is None:
+    if part_mode not in (0, 1, 2):
+        raise ValueError(f"part_mode must be 0, 1 or 2, got {part_mode}")
+    if part_mode:
+        _require_out(part_o, "part_o", (q.shape[1], H * dh), torch.float32, dev)
+        _require_out(part_lse, "part_lse", (q.shape[1], H), torch.float32, dev)
+    if part_mode == 1:
+        out = None
+    elif out is None:
         out = torch.empty(q.shape[1], H * dh, dtype=torch.float16, device=dev)
     # out may be a column slice of a wider context (a head group's columns):
     # rows of H*head_dim contiguous halves at any row stride.
-    if not isinstance(out, torch.Tensor) or out.dtype != torch.float16 or out.device != dev:
-        raise TypeError(f"out must be a float16 tensor on {dev}")
-    if tuple(out.shape) != (q.shape[1], H * dh) or out.stride(1) != 1 or out.stride(0) < H * dh:
-        raise ValueError(f"out must be [{q.shape[1]}, {H * dh}] with contiguous rows, got "
-                         f"{tuple(out.shape)} strides {out.stride()}")
+    if out is not None:
+        if not isinstance(out, torch.Tensor) or out.dtype != torch.float16 or out.device != dev:
+            raise TypeError(f"out must be a float16 tensor on {dev}")
+        if tuple(out.shape) != (q.shape[1], H * dh) or out.stride(1) != 1 or out.stride(0) < H * dh:
+            raise ValueError(f"out must be [{q.shape[1]}, {H * dh}] with contiguous rows, got "
+                             f"{tuple(out.shape)} strides {out.stride()}")
     for name, t in (("q_cu", q_cu), ("kv_off", kv_off), ("kv_len", kv_len)):
         _require(t, name, torch.int32, dev)
     if kv_off.numel() != B * G or kv_len.numel() != B * G:
         raise ValueError(f"kv_off/kv_len must hold {B}x{G} entries")
     lib = _lib.load()
-    rc = lib.tj_flash_attn_fwd_strided(
+    rc = lib.tj_flash_attn_fwd_partial(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), H, dh, q.shape[1], kv_rows, k.stride(1),
         k.stride(0), G, B, max_q_per_sample, q_cu.data_ptr(), kv_off.data_ptr(),
-        kv_len.data_ptr(), float(scale), 1 if causal else 0, _ptr(q_pos0), out.data_ptr(),
-        out.stride(0), _stream(q),
+        kv_len.data_ptr(), float(scale), 1 if causal else 0, _ptr(q_pos0), _ptr(out),
+        0 if out is None else out.stride(0), _ptr(part_o), _ptr(part_lse), part_mode, _stream(q),
     )
     _lib.check(rc, "flash_attn_fwd")
     return out

@@ -316,22 +316,110 @@ def segment_metadata(counts: torch.Tensor, rank: int, causal: bool):
     return kv_off, kv_len, q_pos0
 
 
+class _KvExchange:
+    """Context parallelism's K/V exchange: two [G][2][H][slab][P] buffers per
+    rank (used by alternate layers), each mapped into every other rank (CUDA
+    IPC), one copy stream per peer, the partial-attention buffers and the
+    one-element barrier tensor."""
+
+    def __init__(self, key, bufs, ptrs, mapped, streams, part_o, part_lse, flag):
+        self.key = key
+        self.bufs = bufs
+        self.ptrs = ptrs          # ptrs[d][i]: address of rank d's buffer i in this process
+        self.mapped = mapped
+        self.streams = streams    # streams[d]: pushes into rank d
+        self.part_o = part_o      # [slab, H*dh] fp32: attention over the rank's own keys
+        self.part_lse = part_lse  # [slab, H] fp32: its log2-sum-exp
+        self.flag = flag
+
+
 class ContextParallelEncoder:
     """Context-parallel forward of one long sequence (batch 1) over a process
     group; each rank passes its chunk x_local [1, S_r, D] and mask_local
     [1, S_r] and gets its chunk of the output.  `slab` is the largest S_r over
-    the ranks (all K/V slabs are padded to it so they can be all-gathered)."""
+    the ranks (all K/V slabs are padded to it).
 
-    def __init__(self, model, group=None) -> None:
+    Per layer, after the QKV projection of its own tokens, each rank pushes its
+    K/V slab ([2][H][slab][P], one contiguous block) into slot `rank` of every
+    peer's K/V buffer with the copy engines over NVLink (CUDA IPC mappings) and,
+    meanwhile, runs attention of its queries over its OWN keys, keeping the
+    partial result (normalised fp32 context + log2-sum-exp).  An all-reduce of
+    one element on the current stream is the barrier after which every peer's
+    K/V has landed; attention over the other ranks' keys then merges with the
+    partial (tj_flash_attn_fwd_partial).  With causal masking the keys of
+    later ranks are all masked and those of earlier ranks all visible, so the
+    second launch walks only the earlier ranks, unmasked.  The K/V buffers
+    alternate between layers: a peer writes a buffer again only after every
+    rank has passed the barrier of the layer in between, by which time this
+    rank's attention over it has finished.
+
+    overlap=False runs the plain form instead: a blocking NCCL all-gather of
+    the K/V slabs, then one attention launch over every rank's keys."""
+
+    def __init__(self, model, group=None, overlap: bool = True) -> None:
         import torch.distributed as dist
 
         self.model = model
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.overlap = bool(overlap)
+        self._ex: Optional[_KvExchange] = None
+        self._turn = 0
+
+    def _exchange_for(self, slab: int, H: int, P: int, dh: int, device) -> _KvExchange:
+        import torch.distributed as dist
+
+        from . import _lib
+
+        key = (slab, H, P, dh, device)
+        if self._ex is not None and self._ex.key == key:
+            return self._ex
+        self.close()
+        bufs = [torch.empty(self.world, 2, H, slab, P, dtype=torch.float16, device=device) for _ in range(2)]
+        mine = [_lib.ipc_export(b.data_ptr()) for b in bufs]
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=self.group)
+        ptrs, mapped = [], {}
+        for d in range(self.world):
+            if d == self.rank:
+                ptrs.append([b.data_ptr() for b in bufs])
+                continue
+            row = []
+            for handle, offset in every[d]:
+                if handle not in mapped:
+                    mapped[handle] = _lib.ipc_open(handle)
+                row.append(mapped[handle] + offset)
+            ptrs.append(row)
+        streams = [torch.cuda.Stream(device) for _ in range(self.world)]
+        part_o = torch.empty(slab, H * dh, dtype=torch.float32, device=device)
+        part_lse = torch.empty(slab, H, dtype=torch.float32, device=device)
+        flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self._ex = _KvExchange(key, bufs, ptrs, list(mapped.values()), streams, part_o, part_lse, flag)
+        self._turn = 0
+        return self._ex
+
+    def close(self) -> None:
+        """Unmaps the peers' K/V buffers (collective: every rank calls it)."""
+        ex = self._ex
+        if ex is None:
+            return
+        import torch.distributed as dist
+
+        from . import _lib
+
+        for s in ex.streams:
+            s.synchronize()
+        torch.cuda.current_stream(ex.flag.device).synchronize()
+        for base in ex.mapped:
+            _lib.ipc_close(base)
+        dist.barrier(group=self.group, device_ids=[ex.flag.device.index])
+        self._ex = None
 
     def forward(self, x_local: torch.Tensor, mask_local: Optional[torch.Tensor], slab: int) -> torch.Tensor:
         import torch.distributed as dist
+
+        from . import _lib
 
         m = self.model
         cfg = m.config
@@ -353,6 +441,7 @@ class ContextParallelEncoder:
             raise ValueError(f"context parallelism needs d_model and ffn_dim that are multiples of 8 "
                              f"(got {D} and {F}); run such a model on one GPU")
         dh = D // H
+        causal = bool(cfg.causal)
         x = x_local.contiguous().view(Sl, D)
         if mask_local is not None:
             mask_u8 = mask_local.contiguous().view(torch.uint8) if mask_local.dtype == torch.bool else mask_local.contiguous()
@@ -362,17 +451,31 @@ class ContextParallelEncoder:
         nv, cu, cnt, orig, inv = kernels.plan_views(plan, 1, Sl)
         counts = torch.empty(self.world, dtype=torch.int32, device=dev)
         dist.all_gather_into_tensor(counts, cnt.contiguous(), group=self.group)
-        kv_off, kv_len, q_pos0 = segment_metadata(counts, self.rank, bool(cfg.causal))
+        kv_off, kv_len, q_pos0 = segment_metadata(counts, self.rank, causal)
+        P = kernels.head_pad(dh)  # heads zero-padded to P halves
+        if self.overlap:
+            ex = self._exchange_for(slab, H, P, dh, dev)
+            own_off = torch.zeros(1, 1, dtype=torch.int32, device=dev)
+            own_len = cnt.view(1, 1).contiguous()
+            # the second launch's keys: every other rank's (causal: the earlier ranks')
+            remote_len = kv_len.clone()
+            if causal:
+                remote_len[:, self.rank:] = 0
+            else:
+                remote_len[:, self.rank] = 0
+            has_remote = self.world > 1 and (not causal or self.rank > 0)
+            seg_bytes = 2 * H * slab * P * 2
+        else:
+            kv_all = torch.empty(self.world, 2, H, slab, P, dtype=torch.float16, device=dev)
 
         a16 = torch.empty(slab, D, dtype=torch.float16, device=dev)
-        P = kernels.head_pad(dh)  # heads zero-padded to P halves
         qkv = torch.empty(3, H, slab, P, dtype=torch.float16, device=dev)
-        kv_all = torch.empty(self.world, 2, H, slab, P, dtype=torch.float16, device=dev)
         ctx = torch.empty(slab, D, dtype=torch.float16, device=dev)
         h16 = torch.empty(slab, F, dtype=torch.float16, device=dev)
         y16 = torch.empty(Sl, D, dtype=torch.float16, device=dev)
         x1 = torch.empty(Sl, D, dtype=torch.float32, device=dev)
         x2 = torch.empty(Sl, D, dtype=torch.float32, device=dev)
+        compute = torch.cuda.current_stream(dev)
 
         # Residual stream as in tj_encoder_forward: layer 0 reads x through the
         # plan's gather map; the out-projection and FFN-out write fp16 (y16) and
@@ -391,9 +494,40 @@ class ContextParallelEncoder:
                                         row_count=nv, sum_out=x2, out=a16)
             kernels.gemm_qkv_headmajor(a16, att._qkv_weight_mixed, att._qkv_bias_mixed, H,
                                        row_count=nv, out=qkv)
-            dist.all_gather_into_tensor(kv_all.view(-1), qkv[1:3].reshape(-1), group=self.group)
-            kernels.flash_attn_fwd(qkv[0], kv_all[:, 0], kv_all[:, 1], cu, kv_off, kv_len, Sl, att.scale,
-                                   causal=bool(cfg.causal), q_pos0=q_pos0, out=ctx, head_dim=dh)
+            if self.overlap:
+                buf = self._turn
+                self._turn ^= 1
+                kv_ready = torch.cuda.Event()
+                kv_ready.record(compute)
+                for d in range(self.world):
+                    if d == self.rank:
+                        continue
+                    st = ex.streams[d]
+                    st.wait_event(kv_ready)
+                    _lib.copy_segments([(ex.ptrs[d][buf] + self.rank * seg_bytes, qkv[1].data_ptr(), seg_bytes)],
+                                       st.cuda_stream)
+                    qkv.record_stream(st)
+                # attention over this rank's own keys while the K/V blocks travel
+                kernels.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, own_off, own_len, Sl, att.scale,
+                                       causal=causal, out=None if has_remote else ctx, head_dim=dh,
+                                       part_o=ex.part_o if has_remote else None,
+                                       part_lse=ex.part_lse if has_remote else None,
+                                       part_mode=1 if has_remote else 0)
+                for d in range(self.world):
+                    if d != self.rank:
+                        compute.wait_stream(ex.streams[d])
+                # completes once every rank's pushes (ordered before it on that
+                # rank's stream) have landed
+                dist.all_reduce(ex.flag, group=self.group)
+                if has_remote:
+                    kv = ex.bufs[buf]
+                    kernels.flash_attn_fwd(qkv[0], kv[:, 0], kv[:, 1], cu, kv_off, remote_len, Sl, att.scale,
+                                           causal=False, out=ctx, head_dim=dh, part_o=ex.part_o,
+                                           part_lse=ex.part_lse, part_mode=2)
+            else:
+                dist.all_gather_into_tensor(kv_all.view(-1), qkv[1:3].reshape(-1), group=self.group)
+                kernels.flash_attn_fwd(qkv[0], kv_all[:, 0], kv_all[:, 1], cu, kv_off, kv_len, Sl, att.scale,
+                                       causal=causal, q_pos0=q_pos0, out=ctx, head_dim=dh)
             kernels.gemm_bias_f16(ctx[:Sl], att._out_weight_mixed, att.out_proj.bias, row_count=nv, out=y16)
             kernels.add_ln_cast_f16(xin, y16, layer.norm2.weight, layer.norm2.bias, layer.norm2.eps,
                                     row_map=in_map, row_count=nv, sum_out=x1, out=a16)

@@ -6,7 +6,9 @@ Checks, on N GPUs over NCCL:
     right-padded masks, whole samples otherwise; 1-3 micro-batches) is
     bit-identical to the whole batch on one GPU;
   * context parallelism: one sequence split into valid-token balanced chunks,
-    K/V all-gathered every layer; the gathered output passes the reference's
+    K/V exchanged every layer (copy-engine pushes overlapped with attention
+    over the own keys, then a merged launch over the others; and the plain
+    NCCL all-gather form); the gathered output passes the reference's
     strict gate against the single-GPU model (non-causal one layer, and
     causal two layers);
   * context parallelism at the long-sequence config (B1 S131072 D1024 H16
@@ -96,19 +98,25 @@ def main() -> int:
             ranges = sharding.sequence_ranges(mask[0], world)
             slab = max(e - s for s, e in ranges)
             s0, e0 = ranges[rank]
-            cp = sharding.ContextParallelEncoder(model)
-            out_local = cp.forward(x[:, s0:e0].contiguous().to(dev), mask[:, s0:e0].contiguous().to(dev), slab)
-            padded = torch.zeros(1, slab, cfg.d_model, device=dev)
-            padded[:, : e0 - s0] = out_local
-            parts = [torch.empty_like(padded) for _ in range(world)]
-            dist.all_gather(parts, padded)
-            out = torch.cat([parts[r][:, : e - s] for r, (s, e) in enumerate(ranges)], dim=1)
             ref = model(x.to(dev), mask.to(dev))
-            r = oracle.compare_outputs(ref.cpu(), out.cpu())
-            if not r.passed:
-                failures.append(f"context parallel {cfg_t}: {r}")
-            if torch.count_nonzero(out.cpu()[~mask]) != 0:
-                failures.append(f"context parallel {cfg_t}: padded rows not zero")
+            # overlapped K/V exchange (split attention + merge) and the plain
+            # all-gather form; the overlapped one twice, so both K/V buffers are used
+            for overlap, reps in ((True, 2), (False, 1)):
+                cp = sharding.ContextParallelEncoder(model, overlap=overlap)
+                for _ in range(reps):
+                    out_local = cp.forward(x[:, s0:e0].contiguous().to(dev), mask[:, s0:e0].contiguous().to(dev),
+                                           slab)
+                    padded = torch.zeros(1, slab, cfg.d_model, device=dev)
+                    padded[:, : e0 - s0] = out_local
+                    parts = [torch.empty_like(padded) for _ in range(world)]
+                    dist.all_gather(parts, padded)
+                    out = torch.cat([parts[r][:, : e - s] for r, (s, e) in enumerate(ranges)], dim=1)
+                    r = oracle.compare_outputs(ref.cpu(), out.cpu())
+                    if not r.passed:
+                        failures.append(f"context parallel {cfg_t} overlap={overlap}: {r}")
+                    if torch.count_nonzero(out.cpu()[~mask]) != 0:
+                        failures.append(f"context parallel {cfg_t} overlap={overlap}: padded rows not zero")
+                cp.close()
 
         # ---- context parallelism at the long-sequence config ----------------
         # B1 S131072 D1024 H16 F4096, valid length ~ U[0.9S, S]: every rank
@@ -136,6 +144,7 @@ def main() -> int:
         picked[own.to(dev)] = out_local[(check_rows[own] - s0).to(dev)]
         dist.all_reduce(picked)
         picked = picked.cpu()
+        cp.close()
         del model, cp, out_local
         pkg._lib.device_status(torch.cuda.current_stream().cuda_stream)
 

@@ -474,3 +474,57 @@ def test_flash_attention_head_groups_into_strided_context(cuda_pkg):
         k.flash_attn_fwd(qkv[0, h0:h0 + 2], qkv[1:2, h0:h0 + 2].contiguous(), qkv[2:3, h0:h0 + 2].contiguous(),
                          cud, kv_off, kv_len, 300, 0.125, out=ctx[:, h0 * dh:(h0 + 2) * dh])
     assert torch.equal(ctx, full)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dh", [64, 40, 128])
+def test_flash_attention_split_and_merge(cuda_pkg, causal, dh):
+    """Attention split over two launches as context parallelism runs it: the
+    rank's own key segment first (part_mode 1: fp32 partial + log2-sum-exp),
+    then the other segments (part_mode 2: merged into ctx).  Non-causal: the
+    other segments are segments 0 and 2; causal: the own segment is causal in
+    local positions and only the earlier segment 0 follows, unmasked.  Equals
+    one softmax over all keys."""
+    k = cuda_pkg.kernels
+    g = torch.Generator().manual_seed(17 + dh + causal)
+    H, P = 3, k.head_pad(dh)
+    seg_rows = 700
+    lens = [650, 512, 300]   # keys per segment; own segment = 1 (q rows = its tokens)
+    nq = lens[1]
+    kv = torch.zeros(3, 2, H, seg_rows, P)
+    kv[..., :dh] = torch.randn(3, 2, H, seg_rows, dh, generator=g)
+    kv = kv.half().to(DEV)
+    q = kv[1, 0].clone()     # the own tokens' queries: [H, seg_rows, P]
+    q[:, :, :dh] = torch.randn(H, seg_rows, dh, generator=g).half().to(DEV)
+    q_cu = torch.tensor([0, nq], dtype=torch.int32, device=DEV)
+    scale = dh ** -0.5
+    part_o = torch.empty(seg_rows, H * dh, dtype=torch.float32, device=DEV)
+    part_lse = torch.empty(seg_rows, H, dtype=torch.float32, device=DEV)
+    own_off = torch.zeros(1, 1, dtype=torch.int32, device=DEV)
+    own_len = torch.tensor([[lens[1]]], dtype=torch.int32, device=DEV)
+    assert k.flash_attn_fwd(q, kv[1:2, 0], kv[1:2, 1], q_cu, own_off, own_len, nq, scale, causal=causal,
+                            head_dim=dh, part_o=part_o, part_lse=part_lse, part_mode=1) is None
+    remote = [lens[0], 0, 0] if causal else [lens[0], 0, lens[2]]
+    out = k.flash_attn_fwd(q, kv[:, 0], kv[:, 1], q_cu, torch.zeros(1, 3, dtype=torch.int32, device=DEV),
+                           torch.tensor([remote], dtype=torch.int32, device=DEV), nq, scale, head_dim=dh,
+                           part_o=part_o, part_lse=part_lse, part_mode=2)
+    # reference: keys = segment 0, segment 1 (own), segment 2 (non-causal only)
+    segs = [0, 1] if causal else [0, 1, 2]
+    kk = torch.cat([kv[s, 0, :, : lens[s], :dh].float() for s in segs], 1)
+    vv = torch.cat([kv[s, 1, :, : lens[s], :dh].float() for s in segs], 1)
+    sc = q[:, :nq, :dh].float() @ kk.transpose(1, 2) * scale
+    if causal:
+        qp = lens[0] + torch.arange(nq, device=DEV)[:, None]
+        kp = torch.arange(kk.shape[1], device=DEV)[None, :]
+        sc = sc.masked_fill(kp > qp, float("-inf"))
+    ref = (torch.softmax(sc, -1) @ vv).transpose(0, 1).reshape(nq, H * dh)
+    err = (out[:nq].float() - ref).abs()
+    assert torch.isfinite(out[:nq].float()).all()
+    assert float(err.max()) < 4e-3, float(err.max())
+    # the partial alone is attention over the own keys, its lse the log2 denominator
+    so = q[:, :nq, :dh].float() @ kv[1, 0, :, : lens[1], :dh].float().transpose(1, 2) * scale
+    if causal:
+        so = so.masked_fill(torch.arange(lens[1], device=DEV)[None, :] > torch.arange(nq, device=DEV)[:, None],
+                            float("-inf"))
+    lse_ref = torch.logsumexp(so, -1) / 0.6931471805599453  # natural log -> log2
+    assert float((part_lse[:nq] - lse_ref.transpose(0, 1)).abs().max()) < 2e-3

@@ -1,4 +1,5 @@
-"""Host-side multi-GPU logic on CPU: shard ranges, and the context-parallel
+"""Host-side multi-GPU logic on CPU: shard ranges, the output gather's copy
+plan, the split-attention merge formula, and the context-parallel
 decomposition run by two gloo ranks.
 
 The gloo test mirrors what ContextParallelEncoder does on GPUs -- valid-token
@@ -207,3 +208,38 @@ def test_context_parallel_decomposition_two_gloo_ranks(pkg, causal):
         assert exc is None, f"rank {rank}: {exc}"
         assert n_local > 0
         assert err < 1e-5, f"rank {rank}: max abs error {err}"
+
+
+def test_split_attention_merge_formula():
+    """The merge the split attention performs (part_mode 2), restated on CPU:
+    with the first key set's normalised context o1 and base-2 log-sum-exp
+    lse1, and the second set's unnormalised context O2 and sum l2 relative to
+    2^m2, (O2*a + o1*c) / (l2*a + c), a = 2^(m2-M), c = 2^(lse1-M),
+    M = max(m2, lse1), equals one softmax over both sets; an empty set
+    (lse = -inf or l2 = 0) drops out."""
+    g = torch.Generator().manual_seed(0)
+    log2e = 1.4426950408889634
+    for n1, n2 in ((50, 70), (1, 200), (0, 30), (40, 0)):
+        s = torch.randn(n1 + n2, generator=g, dtype=torch.float64) * 4 * log2e  # base-2 scores
+        v = torch.randn(n1 + n2, 8, generator=g, dtype=torch.float64)
+        full = (torch.softmax(s / log2e, 0)[:, None] * v).sum(0)
+        s1, s2, v1, v2 = s[:n1], s[n1:], v[:n1], v[n1:]
+        if n1:
+            m1 = s1.max()
+            l1 = torch.exp2(s1 - m1).sum()
+            o1 = (torch.exp2(s1 - m1)[:, None] * v1).sum(0) / l1
+            lse1 = m1 + torch.log2(l1)
+        else:
+            o1, lse1 = torch.zeros(8, dtype=torch.float64), torch.tensor(float("-inf"), dtype=torch.float64)
+        if n2:
+            m2 = s2.max() - 3.0  # a stale running max, as the kernel keeps it
+            p2 = torch.exp2(s2 - m2)
+            O2, l2 = (p2[:, None] * v2).sum(0), p2.sum()
+            e2 = m2
+        else:
+            O2, l2, e2 = torch.zeros(8, dtype=torch.float64), torch.tensor(0.0, dtype=torch.float64), float("-inf")
+        M = max(float(e2), float(lse1))
+        a = 0.0 if e2 == float("-inf") else 2.0 ** (float(e2) - M)
+        c = 0.0 if float(lse1) == float("-inf") else 2.0 ** (float(lse1) - M)
+        merged = (O2 * a + o1 * c) / (l2 * a + c)
+        torch.testing.assert_close(merged, full, rtol=1e-12, atol=1e-12)
