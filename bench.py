@@ -25,7 +25,9 @@ The same JSON line nests, measured in the same run at the same N:
                      N ranks (context parallel; the plain model at N=1), with
                      peak memory per GPU;
   sustained          >= 3 s of back-to-back headline steps with the SM clock
-                     sampled, against the sustained tensor peak.
+                     sampled, against the sustained tensor peak;
+  official_shapes    (N=1) the reference's official shapes #1-#13, each gated
+                     and timed, with the ratio to its published RTX 5090 numbers.
 Every timed workload except the long sequence is first gated against the CPU
 FP32 oracle on one sample of the timed input (the reference's strict gate); a
 failure stops the run before any timing (torch_transformer_benchmark.py:725-728).
@@ -77,6 +79,15 @@ for _sid, _b, _d, _h, _s, _l, _f in REFERENCE_SHAPES:
     WORKLOADS[f"ref{_sid}"] = (_b, _s, _d, _h, _f, _l, True, 0.0, False,
                                f"reference official shape #{_sid}: B={_b} S={_s} d_model={_d} H={_h} "
                                f"FFN={_f} layers={_l} causal, no padding")
+
+# The reference's published throughput (tokens/s, B*S basis) for its official
+# shapes on one RTX 5090: results/final/main_shapes_1_13.csv (optimized_throughput)
+# and results/final/main_shape14_summary.json (#14).
+PUBLISHED_RTX5090 = {
+    1: 60995948.61, 2: 1155401.48, 3: 4621605.94, 4: 18317114.73, 5: 77929982.39, 6: 50831314.74,
+    7: 73268458.91, 8: 2932400.22, 9: 54151242.44, 10: 58340931.34, 11: 44046799.59, 12: 18653453.54,
+    13: 60721063.02, 14: 457962.98,
+}
 
 # Workloads whose global batch is split over the ranks (strong scaling, output gather timed).
 SPLIT_BATCH = ("batch",)
@@ -337,9 +348,11 @@ def run_ours(args, world, rank, local):
                 dense = measure_headline(pkg, argparse.Namespace(**{**vars(args), "workload": "dense"}), world,
                                          rank, local, device, nested=True)
                 cp = measure_long(pkg, args, world, rank, local, device, headline=False)
+                shapes = measure_official_shapes(pkg, args, device) if world == 1 else None
                 if rank == 0:
                     line["dense_b8_s2048"] = dense
                     line["context_parallel"] = cp
+                    line["official_shapes"] = shapes
     finally:
         if world > 1:
             import torch.distributed as dist
@@ -451,6 +464,42 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
             cpu = cpu_baseline(args.workload, budget_s=args.cpu_budget)
         line["cpu_baseline"] = cpu
     return line
+
+
+def measure_official_shapes(pkg, args, device):
+    """The reference's official shapes #1-#13 (causal, no padding, 4 layers;
+    tools/matrix_runner.py:49-64) on this GPU: each gated on sample 0 against
+    the FP32 oracle (the accuracy check the reference's runner makes before
+    timing a shape), then K forwards timed back to back with CUDA events, and
+    the ratio to the reference's published RTX 5090 throughput.  #14 (13 GB of
+    input) runs with --workload ref14."""
+    rows = []
+    for sid in range(1, 14):
+        case = Case(f"ref{sid}", 0, 1)
+        cfg = case.cfg_global
+        model = case.model(pkg, device)
+        x = case.x.to(device)
+        m = case.mask.to(device)
+        with torch.inference_mode():
+            for _ in range(args.warmup):
+                out = model(x, m)
+            torch.cuda.synchronize(device)
+            gate = accuracy_gate(out[0], case, 0, f"ref{sid}", 1)
+            if not gate["passed"]:
+                raise SystemExit(f"accuracy gate failed at official shape #{sid}, refusing to time: {gate}")
+            steps = max(args.steps, 20)
+            ms_total, _, _ = timed(lambda i: model(x, m), steps, 1, device, sample_clocks=False)
+        ms = ms_total / steps
+        value = cfg.batch_size * cfg.seq_len / (ms / 1e3)
+        rows.append({"shape": sid, "B": cfg.batch_size, "S": cfg.seq_len, "d_model": cfg.d_model,
+                     "heads": cfg.num_heads, "ffn_dim": cfg.ffn_dim, "layers": cfg.num_layers, "ms": ms,
+                     "tokens_per_s": value, "reference_rtx5090_tokens_per_s": PUBLISHED_RTX5090[sid],
+                     "ratio": value / PUBLISHED_RTX5090[sid], "gate_max_abs": gate["max_abs_error"]})
+        del model, x, m, out
+    ratios = [r["ratio"] for r in rows]
+    return {"shapes": rows, "geomean_ratio_1_13": math.exp(sum(math.log(r) for r in ratios) / len(ratios)),
+            "note": "ratio = tokens/s here / the reference's published RTX 5090 tokens/s "
+                    "(results/final/main_shapes_1_13.csv); every shape gated on sample 0 first"}
 
 
 def launches_per_step(case, gather, micro_batches):
