@@ -320,6 +320,15 @@ typedef struct tj_copy_segment {
  * copy engines over NVLink; no kernel is launched. */
 TJ_API int tj_copy_segments(const tj_copy_segment* segs, int n, void* stream);
 
+/* Enables (1, the default) or disables (0) the fused path of
+ * tj_encoder_forward for small models: sequences of at most 128 tokens,
+ * d_model and ffn_dim at most 128, at most 8 layers, where one CTA runs every
+ * layer of one sample (the reference's official 128-token shapes are this
+ * size).  Results agree with the layer-by-layer path within fp16 rounding
+ * (different accumulation order).  Returns the previous setting; process-wide.
+ * No reference counterpart (the reference fuses these with torch.compile). */
+TJ_API int tj_set_small_encoder(int enabled);
+
 /* ---- encoder without a caller workspace --------------------------------- */
 
 /* Size of the library's static device workspace used by

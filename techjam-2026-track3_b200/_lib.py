@@ -81,6 +81,7 @@ SIGNATURES = {
     "tj_get_last_error": (c_int, [ctypes.c_char_p, ctypes.c_size_t]),
     "tj_set_sync_check": (c_int, [c_int]),
     "tj_device_status": (c_int, [ctypes.POINTER(c_int), c_vp]),
+    "tj_set_small_encoder": (c_int, [c_int]),
     "tj_debug_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
     "tj_debug_withhold_arrive": (c_int, [c_int]),
     "tj_token_plan_ints": (c_i64, [c_int, c_int]),

@@ -15,6 +15,7 @@
 #include "plan_layernorm.cu"
 #include "gemm_tcgen05.cu"
 #include "attention_tcgen05.cu"
+#include "small_encoder.cu"
 
 namespace tj {
 
@@ -140,6 +141,8 @@ int tj_device_status(int* out4, void* stream) {
   }
   return TJ_OK;
 }
+
+int tj_set_small_encoder(int enabled) { return set_small_encoder(enabled); }
 
 int tj_debug_set_wait_limit_ns(uint64_t ns) {
   int rc = check_device();
@@ -406,6 +409,10 @@ int tj_encoder_forward(const tj_encoder_desc* d, const tj_layer_weights* layers,
     return set_error(TJ_ERR_UNSUPPORTED, "encoder_forward: B*S too large");
   const int rows = B * S;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Small models (S <= 128, d_model and ffn_dim <= 128): one fused kernel,
+  // one CTA per sample through every layer (small_encoder.cu).
+  if (small_encoder_fits(d))
+    return finish(launch_small_encoder(d, layers, final_gamma, final_beta, x, mask, out, s), s);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   PlanView plan{reinterpret_cast<int32_t*>(ws + w.plan), B, S};
   __half* a16 = reinterpret_cast<__half*>(ws + w.a16);
