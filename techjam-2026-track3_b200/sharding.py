@@ -75,7 +75,10 @@ def balanced_assignment(lengths: Sequence[int], world: int, d_model: int, ffn_di
     assignment).  A sample of L valid tokens costs L (projections, per
     token) + w * L^2 (attention), w = attention FLOPs per token pair over
     projection FLOPs per token, doubled because attention runs at about half
-    the projections' tensor-core rate.  Returns sorted index lists."""
+    the projections' tensor-core rate.  Each rank's list is in decreasing
+    order of cost (ties by index), so when a rank runs its samples in
+    micro-batches the last one -- whose output gather nothing overlaps -- holds
+    its cheapest samples."""
     B = len(lengths)
     caps = [e - s for s, e in batch_ranges(B, world)]
     w = 2.0 * (4.0 * d_model) / (8.0 * d_model * d_model + 4.0 * d_model * ffn_dim)
@@ -86,7 +89,7 @@ def balanced_assignment(lengths: Sequence[int], world: int, d_model: int, ffn_di
         r = min((r for r in range(world) if len(out[r]) < caps[r]), key=lambda r: (load[r], r))
         out[r].append(i)
         load[r] += cost[i]
-    return [sorted(o) for o in out]
+    return [sorted(o, key=lambda i: (-cost[i], i)) for o in out]
 
 
 def micro_batch_ranges(n: int, parts: int) -> List[Tuple[int, int]]:

