@@ -320,7 +320,7 @@ typedef struct tj_copy_segment {
  * copy engines over NVLink; no kernel is launched. */
 TJ_API int tj_copy_segments(const tj_copy_segment* segs, int n, void* stream);
 
-/* Enables (1, the default) or disables (0) the fused path of
+/* Enables (1) or disables (0, the default) the fused path of
  * tj_encoder_forward for small models: sequences of at most 128 tokens,
  * d_model and ffn_dim at most 128, at most 8 layers, where one CTA runs every
  * layer of one sample (the reference's official 128-token shapes are this

@@ -587,7 +587,9 @@ __global__ void __launch_bounds__(kSmallThreads, 1) small_encoder_kernel(const _
   }
 }
 
-static bool g_small_enabled = true;
+// Off by default: the single-CTA path is still slower than the layer-by-layer
+// kernels on the shapes measured (its per-sample latency is not yet hidden).
+static bool g_small_enabled = false;
 
 bool small_encoder_fits(const tj_encoder_desc* d) {
   if (!g_small_enabled) return false;
