@@ -613,7 +613,10 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
     x_host = [x_cpu.clone().pin_memory() for _ in range(nbuf)]
     m_host = mask_cpu.pin_memory()
     out_host = [torch.empty_like(x_cpu).pin_memory() for _ in range(nbuf)]
-    x_dev = [torch.empty_like(x_cpu, device=device) for _ in range(nbuf)]
+    x_dev = [torch.zeros_like(x_cpu, device=device) for _ in range(nbuf)]
+    # Right-padded masks: upload only each sample's valid rows, the rows the
+    # layer reads (its output at padded rows is zero whatever x holds there).
+    local_lengths = [int(lengths[b]) for b in case.mine] if lengths is not None else None
     m_dev = [torch.empty_like(mask_cpu, device=device) for _ in range(nbuf)]
     outs = [None] * nbuf
     compute = torch.cuda.current_stream(device)
@@ -636,7 +639,12 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
                 b = i % nbuf
                 h2d.wait_event(fwd_done[b])  # buffer b's previous forward has read x_dev[b]
                 with torch.cuda.stream(h2d):
-                    x_dev[b].copy_(x_host[b], non_blocking=True)
+                    if local_lengths is None:
+                        x_dev[b].copy_(x_host[b], non_blocking=True)
+                    else:
+                        for j, n in enumerate(local_lengths):
+                            if n:
+                                x_dev[b][j, :n].copy_(x_host[b][j, :n], non_blocking=True)
                     m_dev[b].copy_(m_host, non_blocking=True)
                 up_done[b].record(h2d)
             if 1 <= i <= n:  # forward step i-1
@@ -691,9 +699,12 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
         "unit": "tokens/s",
         "ms_per_step": ms,
         "steps": steps,
-        "h2d_bytes_per_step": x_cpu.numel() * 4 + mask_cpu.numel(),
+        "h2d_bytes_per_step": (x_cpu.numel() if local_lengths is None else sum(local_lengths) * x_cpu.shape[-1]) * 4
+                              + mask_cpu.numel(),
         "d2h_bytes_per_step": x_cpu.numel() * 4,
         "bytes_per": "rank (each rank uploads its share and downloads its share of the gathered output)",
+        "upload": ("the valid rows of x (the rows the layer reads) and the mask" if local_lengths is not None
+                   else "x and the mask"),
         "pinned_copy_gbs_rank0": {k: round(v, 1) for k, v in bw.items()},
         "pipeline": "upload i+1 / forward i / download i-1 overlapped on 3 streams",
     }

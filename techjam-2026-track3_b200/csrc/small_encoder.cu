@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1) small_encoder_kernel(const _
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               const int d = d0 + i;
-              f[i] = (row < S && d < p.dh) ? __uint_as_float(v[i]) + bias[d] : 0.f;
+              f[i] = (row_valid && d < p.dh) ? __uint_as_float(v[i]) + bias[d] : 0.f;
             }
             if (part < 2) {
               uint8_t* dst = part == 0 ? sQ : sK;
