@@ -13,8 +13,8 @@ with lengths ~ U[1024, 4096], LayerNorm gamma ~ 1+0.02N(0,1), beta ~
 0.02N(0,1), seeded default-init weights.  The batch is split over the N
 ranks (one process per GPU, torchrun, NCCL), B/N samples each balanced by
 work; a step is the forward of every rank's share AND the output gather
-(every rank ends with the [B, S, D] output: copy-engine pushes of valid rows
-over NVLink, overlapped with the next micro-batch), timed together, so the
+(every rank ends with the [B, S, D] output: a push kernel stores the valid
+rows over NVLink, overlapped with the next micro-batch), timed together, so the
 curve over N is strong scaling with the gather inside.  The step time is the
 max over ranks of the CUDA-event time of the K timed steps.
 
@@ -439,7 +439,7 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
         "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
         "config": workload_config(args.workload),
         "parallelism": (f"batch split x{world}: {B // world} samples per GPU balanced by work; the step includes "
-                        "the output gather (valid rows pushed by the copy engines over NVLink into every "
+                        "the output gather (valid rows pushed by a kernel over NVLink into every "
                         f"GPU's [B,S,D] output, {args.micro_batches} micro-batches overlapping it)"
                         if gather else
                         (f"batch split x{world}" if case.split else
@@ -504,12 +504,12 @@ def measure_official_shapes(pkg, args, device):
 
 def launches_per_step(case, gather, micro_batches):
     """Our kernels per step: per forward the token plan, 7 per layer and the
-    final LayerNorm (the gather's copies run on the copy engines)."""
+    final LayerNorm; with the gather, one push kernel per micro-batch."""
     from techjam_b200 import sharding
 
     L = case.cfg_global.num_layers
     forwards = len(sharding.micro_batch_ranges(len(case.mine), micro_batches)) if gather else (1 if case.mine else 0)
-    return forwards * (2 + 7 * L)
+    return forwards * (2 + 7 * L + (1 if gather else 0))
 
 
 def measure_sustained(step, ms_step, world, device, local, flops_step):
@@ -523,8 +523,8 @@ def measure_sustained(step, ms_step, world, device, local, flops_step):
     tflops = flops_step / (ms / 1e3) / 1e12
     sus = peaks.get("bf16_tflops_sustained", PEAK_FALLBACK["bf16_tflops_sustained"])
     return {"steps": n, "seconds": ms_total / 1e3, "ms_per_step": ms, "tflops_valid": tflops,
-            "frac_of_sustained_peak": tflops / sus, "sustained_peak_tflops": sus, "peak_source": kind,
-            "clocks": clocks}
+            "tflops_valid_per_gpu": tflops / world, "frac_of_sustained_peak": tflops / world / sus,
+            "sustained_peak_tflops_per_gpu": sus, "peak_source": kind, "clocks": clocks}
 
 
 def measure_long(pkg, args, world, rank, local, device, headline):

@@ -289,8 +289,8 @@ TJ_API int tj_encoder_forward(const tj_encoder_desc* desc, const tj_layer_weight
  * batch split (balanced sample ranges, candidates/v19/parallel_batch_common.py:31-51)
  * is what these entry points scale out.  A batch split over the GPUs of one
  * node ends with the output gather: each rank pushes the valid rows of its
- * finished samples into every rank's [B, S, D] output with the copy engines,
- * over NVLink, while its next micro-batch computes.  The library does not
+ * finished samples into every rank's [B, S, D] output over NVLink
+ * (tj_push_segments), while its next micro-batch computes.  The library does not
  * allocate: the caller exports its own buffers and maps the peers'. */
 
 #define TJ_IPC_HANDLE_BYTES 64
@@ -319,6 +319,24 @@ typedef struct tj_copy_segment {
  * zero fill, src == NULL) per segment.  Copies to a peer mapping run on the
  * copy engines over NVLink; no kernel is launched. */
 TJ_API int tj_copy_segments(const tj_copy_segment* segs, int n, void* stream);
+
+#define TJ_PUSH_MAX_DST 8
+#define TJ_PUSH_MAX_SEGS 64
+
+typedef struct tj_push_segment {
+  int64_t dst_offset;  /* byte offset inside every destination buffer */
+  const void* src;     /* device address of the bytes to send */
+  int64_t bytes;
+} tj_push_segment;
+
+/* One kernel on `stream` that copies every segment to dst_offset of each of
+ * the num_dst destination buffers (this GPU's own or peers' mappings from
+ * tj_ipc_open): one 16-byte load per unit, one store per destination, the
+ * stores fenced at system scope before the kernel ends.  Sources, offsets and
+ * sizes must be 16-byte aligned; `blocks` is the total CTA count to spread
+ * over the segments (0 = 4 per segment). */
+TJ_API int tj_push_segments(void* const* dst_bases, int num_dst, const tj_push_segment* segs, int num_segs,
+                            int blocks, void* stream);
 
 /* Enables (1) or disables (0, the default) the fused path of
  * tj_encoder_forward for small models: sequences of at most 128 tokens,

@@ -55,6 +55,12 @@ class CopySegment(ctypes.Structure):
 
 
 TJ_IPC_HANDLE_BYTES = 64
+TJ_PUSH_MAX_DST = 8
+TJ_PUSH_MAX_SEGS = 64
+
+
+class PushSegment(ctypes.Structure):
+    _fields_ = [("dst_offset", c_i64), ("src", c_vp), ("bytes", c_i64)]
 
 
 class LayerWeights(ctypes.Structure):
@@ -140,6 +146,7 @@ SIGNATURES = {
     "tj_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
     "tj_ipc_close": (c_int, [c_vp]),
     "tj_copy_segments": (c_int, [ctypes.POINTER(CopySegment), c_int, c_vp]),
+    "tj_push_segments": (c_int, [ctypes.POINTER(c_vp), c_int, ctypes.POINTER(PushSegment), c_int, c_int, c_vp]),
     "tj_encoder_forward_noalloc": (
         c_int,
         [ctypes.POINTER(EncoderDesc), ctypes.POINTER(LayerWeights), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
@@ -249,3 +256,19 @@ def copy_segments(segments, stream: int) -> None:
         arr[i].src = src or None
         arr[i].bytes = nbytes
     check(load().tj_copy_segments(arr, n, c_vp(stream)), "copy_segments")
+
+
+def push_segments(dst_bases, segments, stream: int, blocks: int = 0) -> None:
+    """One kernel copying each (dst_offset, src, bytes) segment to every
+    destination base address (at most TJ_PUSH_MAX_SEGS per call)."""
+    if not segments:
+        return
+    dst = (c_vp * len(dst_bases))(*dst_bases)
+    for i in range(0, len(segments), TJ_PUSH_MAX_SEGS):
+        part = segments[i : i + TJ_PUSH_MAX_SEGS]
+        arr = (PushSegment * len(part))()
+        for k, (off, src, nbytes) in enumerate(part):
+            arr[k].dst_offset = off
+            arr[k].src = src
+            arr[k].bytes = nbytes
+        check(load().tj_push_segments(dst, len(dst_bases), arr, len(part), blocks, c_vp(stream)), "push_segments")

@@ -8,7 +8,7 @@ One process per GPU (torchrun), torch.distributed for the plumbing.
   candidates/v19/parallel_batch_common.py:31-51) or, balanced by estimated
   work rather than count, the sample set of `balanced_assignment`, with no
   data-path collective in the forward itself; `BatchShardedEncoder.forward(
-  ..., gather=True)` ends with the output gather: copy-engine pushes of the
+  ..., gather=True)` ends with the output gather: a push kernel stores the
   valid rows of every finished micro-batch into every rank's [B, S, D]
   output over NVLink (peer mappings), overlapped with the next micro-batch.
 * Context parallelism for one long sequence: rank g holds a contiguous chunk
@@ -134,15 +134,14 @@ def zero_fill_segments(valid_lengths: Sequence[int], seq_len: int, row_bytes: in
 
 class _Exchange:
     """A few [B, S, D] fp32 output buffers per rank (used in turn), each mapped
-    into every other rank of the group (CUDA IPC), plus one copy stream per
-    destination."""
+    into every other rank of the group (CUDA IPC), plus the push stream."""
 
     def __init__(self, key, bufs, ptrs, mapped, streams, flag):
         self.key = key
         self.bufs = bufs          # this rank's output buffers
         self.ptrs = ptrs          # ptrs[d][i]: address of rank d's buffer i in this process
         self.mapped = mapped      # peer allocation bases opened here (closed on release)
-        self.streams = streams    # streams[d]: copies into rank d
+        self.streams = streams    # [the high-priority push stream]
         self.flag = flag          # one-element tensor all-reduced as the completion barrier
 
 
@@ -152,9 +151,10 @@ class BatchShardedEncoder:
 
     forward(..., gather=True) also gathers the [B, S, D] output of the whole
     batch on every rank.  The samples run in micro-batches; as soon as one
-    micro-batch is finished, the copy engines push the valid rows of its
-    samples into every rank's output buffer over NVLink (peer mappings, no
-    SM time, no padded rows on the link) while the next micro-batch computes.
+    micro-batch is finished, one small kernel on a high-priority side stream
+    (tj_push_segments) stores the valid rows of its samples into every rank's
+    output buffer over NVLink (peer mappings; no padded rows on the link)
+    while the next micro-batch computes.
     Each rank zero-fills the padded rows of its own buffer, and an all-reduce
     of one element on the current stream, after this rank's last push, is the
     barrier after which every rank's buffer is complete.
@@ -166,14 +166,17 @@ class BatchShardedEncoder:
     clone it to keep it longer.  Call `close()` (on every rank) before the
     process group goes away."""
 
-    def __init__(self, model, group=None, micro_batches: int = 2, buffers: int = 2) -> None:
+    def __init__(self, model, group=None, micro_batches: int = 2, buffers: int = 2, push_blocks: int = 32) -> None:
         import torch.distributed as dist
 
         self.model = model
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if self.world > 8:
+            raise ValueError("the output gather pushes to at most 8 GPUs (one node)")
         self.micro_batches = max(1, int(micro_batches))
+        self.push_blocks = int(push_blocks)
         if buffers < 2:
             raise ValueError("the gather needs at least two output buffers")
         self.buffers = int(buffers)
@@ -239,7 +242,9 @@ class BatchShardedEncoder:
                     mapped[handle] = _lib.ipc_open(handle)
                 row.append(mapped[handle] + offset)
             ptrs.append(row)
-        streams = [torch.cuda.Stream(device) for _ in range(self.world)]
+        # one high-priority stream: its push kernel's CTAs are scheduled ahead
+        # of the next micro-batch's waiting CTAs
+        streams = [torch.cuda.Stream(device, priority=-1)]
         flag = torch.zeros(1, dtype=torch.int32, device=device)
         self._exchange = _Exchange(key, bufs, ptrs, list(mapped.values()), streams, flag)
         self._turn = 0
@@ -286,20 +291,19 @@ class BatchShardedEncoder:
             base = ex.ptrs[self.rank][buf]
             _lib.copy_segments([(base + off, 0, n) for off, n in zero_fill_segments(valid_lengths, S, row_bytes)],
                                compute.cuda_stream)
+        push = ex.streams[0]
+        dsts = [ex.ptrs[d][buf] for d in range(self.world)]
         for j0, j1 in micro_batch_ranges(n_local, self.micro_batches):
             out = self.model(x_local[j0:j1], None if mask_local is None else mask_local[j0:j1])
             done = torch.cuda.Event()
             done.record(compute)
             segs = gather_segments(assignment, self.rank, (j0, j1), S, row_bytes, valid_lengths)
             src = out.data_ptr()
-            for d in range(self.world):
-                stream = ex.streams[d]
-                stream.wait_event(done)
-                dst = ex.ptrs[d][buf]
-                _lib.copy_segments([(dst + do, src + so, n) for do, so, n in segs], stream.cuda_stream)
-                out.record_stream(stream)
-        for stream in ex.streams:
-            compute.wait_stream(stream)
+            push.wait_event(done)
+            _lib.push_segments(dsts, [(do, src + so, n) for do, so, n in segs], push.cuda_stream,
+                               blocks=self.push_blocks)
+            out.record_stream(push)
+        compute.wait_stream(push)
         # Completes on a rank only after every rank has reached it, i.e. after
         # every rank's pushes (ordered before it on that rank's stream) landed.
         dist.all_reduce(ex.flag, group=self.group)
@@ -322,15 +326,15 @@ def segment_metadata(counts: torch.Tensor, rank: int, causal: bool):
 class _KvExchange:
     """Context parallelism's K/V exchange: two [G][2][H][slab][P] buffers per
     rank (used by alternate layers), each mapped into every other rank (CUDA
-    IPC), one copy stream per peer, the partial-attention buffers and the
-    one-element barrier tensor."""
+    IPC), the push stream, the partial-attention buffers and the one-element
+    barrier tensor."""
 
     def __init__(self, key, bufs, ptrs, mapped, streams, part_o, part_lse, flag):
         self.key = key
         self.bufs = bufs
         self.ptrs = ptrs          # ptrs[d][i]: address of rank d's buffer i in this process
         self.mapped = mapped
-        self.streams = streams    # streams[d]: pushes into rank d
+        self.streams = streams    # [the high-priority push stream]
         self.part_o = part_o      # [slab, H*dh] fp32: attention over the rank's own keys
         self.part_lse = part_lse  # [slab, H] fp32: its log2-sum-exp
         self.flag = flag
@@ -344,7 +348,8 @@ class ContextParallelEncoder:
 
     Per layer, after the QKV projection of its own tokens, each rank pushes its
     K/V slab ([2][H][slab][P], one contiguous block) into slot `rank` of every
-    peer's K/V buffer with the copy engines over NVLink (CUDA IPC mappings) and,
+    peer's K/V buffer over NVLink (tj_push_segments on a high-priority side
+    stream, CUDA IPC mappings) and,
     meanwhile, runs attention of its queries over its OWN keys, keeping the
     partial result (normalised fp32 context + log2-sum-exp).  An all-reduce of
     one element on the current stream is the barrier after which every peer's
@@ -394,7 +399,7 @@ class ContextParallelEncoder:
                     mapped[handle] = _lib.ipc_open(handle)
                 row.append(mapped[handle] + offset)
             ptrs.append(row)
-        streams = [torch.cuda.Stream(device) for _ in range(self.world)]
+        streams = [torch.cuda.Stream(device, priority=-1)]  # the push stream
         part_o = torch.empty(slab, H * dh, dtype=torch.float32, device=device)
         part_lse = torch.empty(slab, H, dtype=torch.float32, device=device)
         flag = torch.zeros(1, dtype=torch.int32, device=device)
@@ -502,23 +507,19 @@ class ContextParallelEncoder:
                 self._turn ^= 1
                 kv_ready = torch.cuda.Event()
                 kv_ready.record(compute)
-                for d in range(self.world):
-                    if d == self.rank:
-                        continue
-                    st = ex.streams[d]
-                    st.wait_event(kv_ready)
-                    _lib.copy_segments([(ex.ptrs[d][buf] + self.rank * seg_bytes, qkv[1].data_ptr(), seg_bytes)],
-                                       st.cuda_stream)
-                    qkv.record_stream(st)
+                push = ex.streams[0]
+                push.wait_event(kv_ready)
+                _lib.push_segments([ex.ptrs[d][buf] for d in range(self.world) if d != self.rank],
+                                   [(self.rank * seg_bytes, qkv[1].data_ptr(), seg_bytes)], push.cuda_stream,
+                                   blocks=32)
+                qkv.record_stream(push)
                 # attention over this rank's own keys while the K/V blocks travel
                 kernels.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, own_off, own_len, Sl, att.scale,
                                        causal=causal, out=None if has_remote else ctx, head_dim=dh,
                                        part_o=ex.part_o if has_remote else None,
                                        part_lse=ex.part_lse if has_remote else None,
                                        part_mode=1 if has_remote else 0)
-                for d in range(self.world):
-                    if d != self.rank:
-                        compute.wait_stream(ex.streams[d])
+                compute.wait_stream(ex.streams[0])
                 # completes once every rank's pushes (ordered before it on that
                 # rank's stream) have landed
                 dist.all_reduce(ex.flag, group=self.group)
