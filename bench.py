@@ -369,7 +369,8 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
     cfg = case.cfg_global
     B, S = cfg.batch_size, cfg.seq_len
     model = case.model(pkg, device)
-    encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches)
+    encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches,
+                                           transport=args.gather_transport)
     gather = case.split and world > 1
     lengths = case.lengths if case.right_padded else None
     mask_local = case.mask_local.to(device)
@@ -608,7 +609,8 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
     x_cpu, mask_cpu = case.x_local, case.mask_local
     # three exchange buffers: the download of step i-3 is the last reader of
     # the buffer the gather of step i writes, and it completes before step i-1
-    encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches, buffers=3)
+    encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches, buffers=3,
+                                           transport=args.gather_transport)
     mine = torch.tensor(case.mine, dtype=torch.int64, device=device)
     x_host = [x_cpu.clone().pin_memory() for _ in range(nbuf)]
     m_host = mask_cpu.pin_memory()
@@ -953,6 +955,8 @@ def main():
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="batch")
     ap.add_argument("--micro-batches", type=int, default=2,
                     help="micro-batches per rank in the split-batch gather (overlap of the gather)")
+    ap.add_argument("--gather-transport", choices=("kernel", "copy_engine"), default="kernel",
+                    help="how the output gather moves rows over NVLink")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",

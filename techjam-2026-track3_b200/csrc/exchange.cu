@@ -52,16 +52,32 @@ struct PushParams {
   int64_t units[TJ_PUSH_MAX_SEGS];  // 16-byte units per segment
 };
 
+constexpr int kPushUnroll = 8;  // 16-byte loads in flight per thread
+
 __global__ void __launch_bounds__(256) push_segments_kernel(const __grid_constant__ PushParams p) {
   const int s = blockIdx.y;
   const int64_t n = p.units[s];
   const uint4* src = reinterpret_cast<const uint4*>(p.src[s]);
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < n; u += stride) {
-    const uint4 v = __ldg(src + u);
+  const int64_t tile = (int64_t)blockDim.x * kPushUnroll;
+  // Each thread loads kPushUnroll units (coalesced across the block for each
+  // k) before storing them, so enough bytes are in flight to cover the load
+  // latency and the remote stores stream.
+  for (int64_t base = (int64_t)blockIdx.x * tile; base < n; base += (int64_t)gridDim.x * tile) {
+    uint4 v[kPushUnroll];
+#pragma unroll
+    for (int k = 0; k < kPushUnroll; ++k) {
+      const int64_t u = base + (int64_t)k * blockDim.x + threadIdx.x;
+      if (u < n) v[k] = __ldg(src + u);
+    }
 #pragma unroll 1
-    for (int d = 0; d < p.num_dst; ++d)
-      reinterpret_cast<uint4*>(p.dst[d] + p.dst_off[s])[u] = v;
+    for (int d = 0; d < p.num_dst; ++d) {
+      uint4* dst = reinterpret_cast<uint4*>(p.dst[d] + p.dst_off[s]);
+#pragma unroll
+      for (int k = 0; k < kPushUnroll; ++k) {
+        const int64_t u = base + (int64_t)k * blockDim.x + threadIdx.x;
+        if (u < n) dst[u] = v[k];
+      }
+    }
   }
   // Make the stores visible to the other GPUs before anything ordered after
   // this kernel (the barrier that tells the peers their buffers are complete).

@@ -166,7 +166,8 @@ class BatchShardedEncoder:
     clone it to keep it longer.  Call `close()` (on every rank) before the
     process group goes away."""
 
-    def __init__(self, model, group=None, micro_batches: int = 2, buffers: int = 2, push_blocks: int = 32) -> None:
+    def __init__(self, model, group=None, micro_batches: int = 2, buffers: int = 2, push_blocks: int = 64,
+                 transport: str = "kernel") -> None:
         import torch.distributed as dist
 
         self.model = model
@@ -177,6 +178,9 @@ class BatchShardedEncoder:
             raise ValueError("the output gather pushes to at most 8 GPUs (one node)")
         self.micro_batches = max(1, int(micro_batches))
         self.push_blocks = int(push_blocks)
+        if transport not in ("kernel", "copy_engine"):
+            raise ValueError("transport must be 'kernel' or 'copy_engine'")
+        self.transport = transport
         if buffers < 2:
             raise ValueError("the gather needs at least two output buffers")
         self.buffers = int(buffers)
@@ -242,9 +246,11 @@ class BatchShardedEncoder:
                     mapped[handle] = _lib.ipc_open(handle)
                 row.append(mapped[handle] + offset)
             ptrs.append(row)
-        # one high-priority stream: its push kernel's CTAs are scheduled ahead
-        # of the next micro-batch's waiting CTAs
-        streams = [torch.cuda.Stream(device, priority=-1)]
+        # kernel: one high-priority stream, its push kernel's CTAs scheduled
+        # ahead of the next micro-batch's waiting CTAs; copy engines: one
+        # stream per destination, so the copies run on several engines
+        n_streams = 1 if self.transport == "kernel" else self.world
+        streams = [torch.cuda.Stream(device, priority=-1) for _ in range(n_streams)]
         flag = torch.zeros(1, dtype=torch.int32, device=device)
         self._exchange = _Exchange(key, bufs, ptrs, list(mapped.values()), streams, flag)
         self._turn = 0
@@ -299,11 +305,18 @@ class BatchShardedEncoder:
             done.record(compute)
             segs = gather_segments(assignment, self.rank, (j0, j1), S, row_bytes, valid_lengths)
             src = out.data_ptr()
-            push.wait_event(done)
-            _lib.push_segments(dsts, [(do, src + so, n) for do, so, n in segs], push.cuda_stream,
-                               blocks=self.push_blocks)
-            out.record_stream(push)
-        compute.wait_stream(push)
+            if self.transport == "kernel":
+                push.wait_event(done)
+                _lib.push_segments(dsts, [(do, src + so, n) for do, so, n in segs], push.cuda_stream,
+                                   blocks=self.push_blocks)
+                out.record_stream(push)
+            else:
+                for d, stream in enumerate(ex.streams):
+                    stream.wait_event(done)
+                    _lib.copy_segments([(dsts[d] + do, src + so, n) for do, so, n in segs], stream.cuda_stream)
+                    out.record_stream(stream)
+        for stream in ex.streams:
+            compute.wait_stream(stream)
         # Completes on a rank only after every rank has reached it, i.e. after
         # every rank's pushes (ordered before it on that rank's stream) landed.
         dist.all_reduce(ex.flag, group=self.group)

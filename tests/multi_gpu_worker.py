@@ -80,6 +80,12 @@ def main() -> int:
                                  valid_lengths=lengths)
                 if not torch.equal(out, full):
                     failures.append(f"valid-row gather (micro-batches {mb}, call {rep}) differs from one GPU")
+        # the copy-engine transport of the same gather
+        ce = sharding.BatchShardedEncoder(model, micro_batches=2, transport="copy_engine")
+        out = ce.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign, valid_lengths=lengths)
+        if not torch.equal(out, full):
+            failures.append("copy-engine gather differs from one GPU")
+        ce.close()
         # a non-prefix mask: whole samples are copied
         mask2 = mask.clone()
         mask2[:, 1::3] = False
