@@ -2,12 +2,12 @@
 
 Checks, on N GPUs over NCCL:
   * batch sharding: each rank runs its balanced range of the batch; the
-    gathered output (copy-engine pushes over NVLink; valid rows only for
-    right-padded masks, whole samples otherwise; 1-3 micro-batches) is
+    gathered output (push kernel over NVLink, or copy engines; valid rows only
+    for right-padded masks, whole samples otherwise; 1-3 micro-batches) is
     bit-identical to the whole batch on one GPU;
   * context parallelism: one sequence split into valid-token balanced chunks,
-    K/V exchanged every layer (copy-engine pushes overlapped with attention
-    over the own keys, then a merged launch over the others; and the plain
+    K/V exchanged every layer (push kernel overlapped with attention over
+    the own keys, then a merged launch over the others; and the plain
     NCCL all-gather form); the gathered output passes the reference's
     strict gate against the single-GPU model (non-causal one layer, and
     causal two layers);
