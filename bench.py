@@ -13,8 +13,9 @@ with lengths ~ U[1024, 4096], LayerNorm gamma ~ 1+0.02N(0,1), beta ~
 0.02N(0,1), seeded default-init weights.  The batch is split over the N
 ranks (one process per GPU, torchrun, NCCL), B/N samples each balanced by
 work; a step is the forward of every rank's share AND the output gather
-(every rank ends with the [B, S, D] output: a push kernel stores the valid
-rows over NVLink, overlapped with the next micro-batch), timed together, so the
+(every rank ends with the [B, S, D] output: the valid rows are pushed over
+NVLink by the copy engines, overlapped with the next micro-batch), timed
+together, so the
 curve over N is strong scaling with the gather inside.  The step time is the
 max over ranks of the CUDA-event time of the K timed steps.
 
@@ -440,8 +441,9 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
         "data": "synthetic (seeded N(0,1) inputs, default-init weights, right-padded masks)",
         "config": workload_config(args.workload),
         "parallelism": (f"batch split x{world}: {B // world} samples per GPU balanced by work; the step includes "
-                        "the output gather (valid rows pushed by a kernel over NVLink into every "
-                        f"GPU's [B,S,D] output, {args.micro_batches} micro-batches overlapping it)"
+                        "the output gather (valid rows pushed over NVLink into every "
+                        f"GPU's [B,S,D] output, {encoder.micro_batches} micro-batches overlapping it, "
+                        f"transport: {encoder.transport})"
                         if gather else
                         (f"batch split x{world}" if case.split else
                          f"x{world}: each GPU runs its own batch of {B} (weak scaling, no collective)")),
@@ -452,7 +454,8 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
                   for r, p in enumerate(per_rank)],
         "tflops_valid": flops_step / (ms_step / 1e3) / 1e12,
         "accuracy_gate": gate,
-        "gpu_launches": launches_per_step(case, gather, args.micro_batches) * args.steps,
+        "gpu_launches": launches_per_step(case, gather, encoder.micro_batches,
+                                          encoder.transport == "kernel") * args.steps,
         "roofline": roof,
         "kernels": kernels,
         "clocks": clocks,
@@ -503,14 +506,14 @@ def measure_official_shapes(pkg, args, device):
                     "(results/final/main_shapes_1_13.csv); every shape gated on sample 0 first"}
 
 
-def launches_per_step(case, gather, micro_batches):
+def launches_per_step(case, gather, micro_batches, push_kernel):
     """Our kernels per step: per forward the token plan, 7 per layer and the
-    final LayerNorm; with the gather, one push kernel per micro-batch."""
+    final LayerNorm; with the kernel transport, one push kernel per micro-batch."""
     from techjam_b200 import sharding
 
     L = case.cfg_global.num_layers
     forwards = len(sharding.micro_batch_ranges(len(case.mine), micro_batches)) if gather else (1 if case.mine else 0)
-    return forwards * (2 + 7 * L + (1 if gather else 0))
+    return forwards * (2 + 7 * L + (1 if gather and push_kernel else 0))
 
 
 def measure_sustained(step, ms_step, world, device, local, flops_step):
@@ -953,9 +956,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="batch")
-    ap.add_argument("--micro-batches", type=int, default=2,
-                    help="micro-batches per rank in the split-batch gather (overlap of the gather)")
-    ap.add_argument("--gather-transport", choices=("kernel", "copy_engine"), default="kernel",
+    ap.add_argument("--micro-batches", type=int, default=0,
+                    help="micro-batches per rank in the split-batch gather (0 = 2 up to 2 GPUs, 4 above)")
+    ap.add_argument("--gather-transport", choices=("kernel", "copy_engine"), default="copy_engine",
                     help="how the output gather moves rows over NVLink")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -4,10 +4,11 @@
 //
 // The gather itself is host-orchestrated (sharding.py): every rank pushes the
 // valid rows of each finished sample straight into the output buffer of every
-// rank with tj_push_segments (one small kernel, stores over NVLink), so the
-// bytes cross NVLink once and the transfer overlaps the next micro-batch's
-// kernels.  Padded rows never cross the link; each receiver zero-fills them
-// locally.  tj_copy_segments (copy engines) serves the zero fills.
+// rank, so the bytes cross NVLink once and the transfer overlaps the next
+// micro-batch's kernels.  Two transports: tj_copy_segments (copy engines, one
+// stream per destination; the default, measured faster) and tj_push_segments
+// (one small kernel storing over NVLink).  Padded rows never cross the link;
+// each receiver zero-fills them locally with tj_copy_segments.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <string.h>

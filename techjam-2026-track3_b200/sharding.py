@@ -8,9 +8,9 @@ One process per GPU (torchrun), torch.distributed for the plumbing.
   candidates/v19/parallel_batch_common.py:31-51) or, balanced by estimated
   work rather than count, the sample set of `balanced_assignment`, with no
   data-path collective in the forward itself; `BatchShardedEncoder.forward(
-  ..., gather=True)` ends with the output gather: a push kernel stores the
-  valid rows of every finished micro-batch into every rank's [B, S, D]
-  output over NVLink (peer mappings), overlapped with the next micro-batch.
+  ..., gather=True)` ends with the output gather: the valid rows of every
+  finished micro-batch go into every rank's [B, S, D] output over NVLink
+  (copy engines into peer mappings), overlapped with the next micro-batch.
 * Context parallelism for one long sequence: rank g holds a contiguous chunk
   of the sequence.  Attention is the only op that mixes tokens, so each rank
   computes LN1 and the QKV projection for its own tokens, all-gathers the
@@ -134,14 +134,14 @@ def zero_fill_segments(valid_lengths: Sequence[int], seq_len: int, row_bytes: in
 
 class _Exchange:
     """A few [B, S, D] fp32 output buffers per rank (used in turn), each mapped
-    into every other rank of the group (CUDA IPC), plus the push stream."""
+    into every other rank of the group (CUDA IPC), plus the transfer streams."""
 
     def __init__(self, key, bufs, ptrs, mapped, streams, flag):
         self.key = key
         self.bufs = bufs          # this rank's output buffers
         self.ptrs = ptrs          # ptrs[d][i]: address of rank d's buffer i in this process
         self.mapped = mapped      # peer allocation bases opened here (closed on release)
-        self.streams = streams    # [the high-priority push stream]
+        self.streams = streams    # copy engines: streams[d] copies into rank d; kernel: [the push stream]
         self.flag = flag          # one-element tensor all-reduced as the completion barrier
 
 
@@ -151,10 +151,11 @@ class BatchShardedEncoder:
 
     forward(..., gather=True) also gathers the [B, S, D] output of the whole
     batch on every rank.  The samples run in micro-batches; as soon as one
-    micro-batch is finished, one small kernel on a high-priority side stream
-    (tj_push_segments) stores the valid rows of its samples into every rank's
-    output buffer over NVLink (peer mappings; no padded rows on the link)
-    while the next micro-batch computes.
+    micro-batch is finished, the valid rows of its samples go into every
+    rank's output buffer over NVLink (peer mappings; no padded rows on the
+    link) while the next micro-batch computes: by the copy engines (default,
+    one stream per destination) or by one push kernel on a high-priority side
+    stream (transport="kernel", tj_push_segments; measured slower on B200s).
     Each rank zero-fills the padded rows of its own buffer, and an all-reduce
     of one element on the current stream, after this rank's last push, is the
     barrier after which every rank's buffer is complete.
@@ -166,8 +167,8 @@ class BatchShardedEncoder:
     clone it to keep it longer.  Call `close()` (on every rank) before the
     process group goes away."""
 
-    def __init__(self, model, group=None, micro_batches: int = 2, buffers: int = 2, push_blocks: int = 64,
-                 transport: str = "kernel") -> None:
+    def __init__(self, model, group=None, micro_batches: Optional[int] = None, buffers: int = 2,
+                 push_blocks: int = 64, transport: str = "copy_engine") -> None:
         import torch.distributed as dist
 
         self.model = model
@@ -176,7 +177,8 @@ class BatchShardedEncoder:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         if self.world > 8:
             raise ValueError("the output gather pushes to at most 8 GPUs (one node)")
-        self.micro_batches = max(1, int(micro_batches))
+        # measured on B200s (B32 S4096): 2 micro-batches best at 2 GPUs, 4 from 4 GPUs up
+        self.micro_batches = max(1, int(micro_batches)) if micro_batches else (2 if self.world <= 2 else 4)
         self.push_blocks = int(push_blocks)
         if transport not in ("kernel", "copy_engine"):
             raise ValueError("transport must be 'kernel' or 'copy_engine'")
@@ -339,15 +341,15 @@ def segment_metadata(counts: torch.Tensor, rank: int, causal: bool):
 class _KvExchange:
     """Context parallelism's K/V exchange: two [G][2][H][slab][P] buffers per
     rank (used by alternate layers), each mapped into every other rank (CUDA
-    IPC), the push stream, the partial-attention buffers and the one-element
-    barrier tensor."""
+    IPC), one copy stream per peer, the partial-attention buffers and the
+    one-element barrier tensor."""
 
     def __init__(self, key, bufs, ptrs, mapped, streams, part_o, part_lse, flag):
         self.key = key
         self.bufs = bufs
         self.ptrs = ptrs          # ptrs[d][i]: address of rank d's buffer i in this process
         self.mapped = mapped
-        self.streams = streams    # [the high-priority push stream]
+        self.streams = streams    # streams[d]: copies into rank d
         self.part_o = part_o      # [slab, H*dh] fp32: attention over the rank's own keys
         self.part_lse = part_lse  # [slab, H] fp32: its log2-sum-exp
         self.flag = flag
@@ -361,8 +363,7 @@ class ContextParallelEncoder:
 
     Per layer, after the QKV projection of its own tokens, each rank pushes its
     K/V slab ([2][H][slab][P], one contiguous block) into slot `rank` of every
-    peer's K/V buffer over NVLink (tj_push_segments on a high-priority side
-    stream, CUDA IPC mappings) and,
+    peer's K/V buffer with the copy engines over NVLink (CUDA IPC mappings) and,
     meanwhile, runs attention of its queries over its OWN keys, keeping the
     partial result (normalised fp32 context + log2-sum-exp).  An all-reduce of
     one element on the current stream is the barrier after which every peer's
@@ -412,7 +413,7 @@ class ContextParallelEncoder:
                     mapped[handle] = _lib.ipc_open(handle)
                 row.append(mapped[handle] + offset)
             ptrs.append(row)
-        streams = [torch.cuda.Stream(device, priority=-1)]  # the push stream
+        streams = [torch.cuda.Stream(device) for _ in range(self.world)]  # streams[d]: pushes into rank d
         part_o = torch.empty(slab, H * dh, dtype=torch.float32, device=device)
         part_lse = torch.empty(slab, H, dtype=torch.float32, device=device)
         flag = torch.zeros(1, dtype=torch.int32, device=device)
@@ -520,19 +521,23 @@ class ContextParallelEncoder:
                 self._turn ^= 1
                 kv_ready = torch.cuda.Event()
                 kv_ready.record(compute)
-                push = ex.streams[0]
-                push.wait_event(kv_ready)
-                _lib.push_segments([ex.ptrs[d][buf] for d in range(self.world) if d != self.rank],
-                                   [(self.rank * seg_bytes, qkv[1].data_ptr(), seg_bytes)], push.cuda_stream,
-                                   blocks=32)
-                qkv.record_stream(push)
+                for d in range(self.world):  # copy engines, one stream per peer
+                    if d == self.rank:
+                        continue
+                    st = ex.streams[d]
+                    st.wait_event(kv_ready)
+                    _lib.copy_segments([(ex.ptrs[d][buf] + self.rank * seg_bytes, qkv[1].data_ptr(), seg_bytes)],
+                                       st.cuda_stream)
+                    qkv.record_stream(st)
                 # attention over this rank's own keys while the K/V blocks travel
                 kernels.flash_attn_fwd(qkv[0], qkv[1:2], qkv[2:3], cu, own_off, own_len, Sl, att.scale,
                                        causal=causal, out=None if has_remote else ctx, head_dim=dh,
                                        part_o=ex.part_o if has_remote else None,
                                        part_lse=ex.part_lse if has_remote else None,
                                        part_mode=1 if has_remote else 0)
-                compute.wait_stream(ex.streams[0])
+                for d in range(self.world):
+                    if d != self.rank:
+                        compute.wait_stream(ex.streams[d])
                 # completes once every rank's pushes (ordered before it on that
                 # rank's stream) have landed
                 dist.all_reduce(ex.flag, group=self.group)

@@ -2,11 +2,11 @@
 
 Checks, on N GPUs over NCCL:
   * batch sharding: each rank runs its balanced range of the batch; the
-    gathered output (push kernel over NVLink, or copy engines; valid rows only
+    gathered output (copy engines over NVLink, or the push kernel; valid rows only
     for right-padded masks, whole samples otherwise; 1-3 micro-batches) is
     bit-identical to the whole batch on one GPU;
   * context parallelism: one sequence split into valid-token balanced chunks,
-    K/V exchanged every layer (push kernel overlapped with attention over
+    K/V exchanged every layer (copy engines overlapped with attention over
     the own keys, then a merged launch over the others; and the plain
     NCCL all-gather form); the gathered output passes the reference's
     strict gate against the single-GPU model (non-causal one layer, and
@@ -80,12 +80,12 @@ def main() -> int:
                                  valid_lengths=lengths)
                 if not torch.equal(out, full):
                     failures.append(f"valid-row gather (micro-batches {mb}, call {rep}) differs from one GPU")
-        # the copy-engine transport of the same gather
-        ce = sharding.BatchShardedEncoder(model, micro_batches=2, transport="copy_engine")
-        out = ce.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign, valid_lengths=lengths)
+        # the push-kernel transport of the same gather
+        pk = sharding.BatchShardedEncoder(model, micro_batches=2, transport="kernel")
+        out = pk.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign, valid_lengths=lengths)
         if not torch.equal(out, full):
-            failures.append("copy-engine gather differs from one GPU")
-        ce.close()
+            failures.append("push-kernel gather differs from one GPU")
+        pk.close()
         # a non-prefix mask: whole samples are copied
         mask2 = mask.clone()
         mask2[:, 1::3] = False
