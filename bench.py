@@ -600,12 +600,16 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
     its input share from pinned host memory to the device, runs the forward
     (and, split over N GPUs, the output gather) and copies this rank's share
     of the output back to pinned host memory, all inside the timed region.
+    With right-padded masks only the valid rows cross the host link in
+    either direction (techjam_b200.hostio): the layer never reads x at a
+    padded row and writes exact zeros there, so the host writes those zero
+    rows of its output itself, inside the timed region too.
     Steps are pipelined the way a serving loop runs them: the upload of step
     i+1 and the download of step i-1 (two copy streams) overlap the forward of
     step i (compute stream), with events ordering each step's three stages.
     The pinned-copy bandwidth of rank 0, measured alone, is reported beside
     it so the host-link limit can be located."""
-    from techjam_b200 import sharding
+    from techjam_b200 import hostio, sharding
 
     steps = max(3, min(args.steps, 60))
     nbuf = 3
@@ -647,9 +651,7 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
                     if local_lengths is None:
                         x_dev[b].copy_(x_host[b], non_blocking=True)
                     else:
-                        for j, n in enumerate(local_lengths):
-                            if n:
-                                x_dev[b][j, :n].copy_(x_host[b][j, :n], non_blocking=True)
+                        hostio.upload_valid_rows(x_host[b], x_dev[b], local_lengths)
                     m_dev[b].copy_(m_host, non_blocking=True)
                 up_done[b].record(h2d)
             if 1 <= i <= n:  # forward step i-1
@@ -662,7 +664,13 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
                 b = (i - 2) % nbuf
                 d2h.wait_event(fwd_done[b])
                 with torch.cuda.stream(d2h):
-                    out_host[b].copy_(outs[b], non_blocking=True)
+                    if local_lengths is None:
+                        out_host[b].copy_(outs[b], non_blocking=True)
+                    else:
+                        # the host zero fill below must not race the previous
+                        # download into the same host buffer
+                        down_done[b].synchronize()
+                        hostio.download_valid_rows(outs[b], out_host[b], local_lengths)
                 outs[b].record_stream(d2h)
                 down_done[b].record(d2h)
 
@@ -683,6 +691,9 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
         end.record(compute)
         torch.cuda.synchronize(device)
         ms = reduce_over_ranks(world, start.elapsed_time(end), device) / steps
+        # the host output of the last step equals the device output it came from
+        last = (steps - 1) % nbuf
+        host_ok = bool(torch.equal(out_host[last], outs[last].cpu()))
         # pinned copy bandwidth of each rank alone (all ranks at once)
         bw = {}
         for name, src, dst in (("h2d", x_host[0], x_dev[0]), ("d2h", x_dev[0], out_host[0])):
@@ -706,11 +717,14 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
         "steps": steps,
         "h2d_bytes_per_step": (x_cpu.numel() if local_lengths is None else sum(local_lengths) * x_cpu.shape[-1]) * 4
                               + mask_cpu.numel(),
-        "d2h_bytes_per_step": x_cpu.numel() * 4,
+        "d2h_bytes_per_step": (x_cpu.numel() if local_lengths is None else sum(local_lengths) * x_cpu.shape[-1]) * 4,
         "bytes_per": "rank (each rank uploads its share and downloads its share of the gathered output)",
         "upload": ("the valid rows of x (the rows the layer reads) and the mask" if local_lengths is not None
                    else "x and the mask"),
+        "download": ("the valid rows of the output; the host writes the zero rows of the padded positions "
+                     "itself (inside the timed region)" if local_lengths is not None else "the whole output"),
         "pinned_copy_gbs_rank0": {k: round(v, 1) for k, v in bw.items()},
+        "host_output_equals_device": host_ok,
         "pipeline": "upload i+1 / forward i / download i-1 overlapped on 3 streams",
     }
 

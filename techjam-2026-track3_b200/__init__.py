@@ -6,6 +6,6 @@ The directory name is not a Python identifier; load it with
 as the importable module `techjam_b200`.
 """
 from .model import TransformerConfig, UserOptimizedTransformer  # noqa: F401
-from . import kernels  # noqa: F401
+from . import hostio, kernels  # noqa: F401
 
-__all__ = ["TransformerConfig", "UserOptimizedTransformer", "kernels"]
+__all__ = ["TransformerConfig", "UserOptimizedTransformer", "hostio", "kernels"]
