@@ -61,6 +61,9 @@ struct GemmKernelParams {
   int ld_resid;
   int heads, head_dim, d_model;
   int head_pad;  // head-major row length (halves) of the QKV output: 64, 128 or 256
+  // 1: the fp16 epilogue stores whole 32-row blocks with TMA (tensor map tmC
+  // of the pair kernel; 64-byte swizzle, 32 x 32 boxes); 0: st.global only.
+  int tma_store;
 };
 
 // Shared-memory scratch of the epilogue warps (one 32-row block each), used to
@@ -136,6 +139,26 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
+// Bulk tensor stores (shared -> global, completion tracked per thread in bulk
+// groups).  The innermost coordinate is a multiple of 32 fp16 elements.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The bulk stores of this thread have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// The bulk stores of this thread are complete (written to global memory).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Epilogue of one accumulator tile for one epilogue warp: its 32 rows (TMEM
 // lane quarter) and its column slice, in 32-column chunks.  Each chunk is
 // read from TMEM with one row per thread, passed through the warp's scratch
@@ -146,12 +169,18 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 //   fp16 (QKV, GELU): lane = (row l/4 + 8i, 8 columns), 64 B per row segment.
 // The residual is prefetched in the store layout before the accumulator is
 // waited for, so its DRAM latency hides behind the tile's main loop.
+// With tmC (the pair kernel, p.tma_store), a full 32-row block of an fp16
+// output leaves the scratch as one bulk tensor store instead: the scratch
+// rows are 64 bytes with the granules XOR-swizzled by (row >> 1) & 3, which is
+// the 64-byte TMA swizzle, and the scratch is 512-byte aligned.  Before the
+// scratch is rewritten, lane 0 waits until its last store has read it.
 // Returns false if the CTA aborts.
 template <int BN, int EPI, int kEpiWarps>
 __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_t tmem_acc, int m0,
                                               int n0, int rows, int quarter, int slice, uint32_t lane,
                                               uint32_t tfull_bar, uint32_t tfull_parity,
-                                              volatile int* abort_flag, uint32_t scratch) {
+                                              volatile int* abort_flag, uint32_t scratch,
+                                              const CUtensorMap* tmC = nullptr) {
   constexpr int kSlices = kEpiWarps / 4;
   constexpr int kChunks = BN / 32 / kSlices;
   const int row_base = m0 + quarter * 32;
@@ -292,10 +321,32 @@ __device__ __forceinline__ bool epilogue_tile(const GemmKernelParams& p, uint32_
         continue;
       }
       // Row-contiguous stores through the scratch: 32 rows x 64 bytes.
+      const bool tma = tmC != nullptr && p.tma_store && row_base + 32 <= rows;  // uniform for the warp
+      if (tmC != nullptr && p.tma_store) {
+        if (lane == 0) bulk_wait_read();  // an earlier bulk store has read the scratch
+        __syncwarp();
+      }
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         st_shared_v4(scratch + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4),
                      make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]));
+      if (tma) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (EPI == kEpiQkvHeadMajor) {
+            // a 32-column chunk lies inside one head (head_dim == head_pad here)
+            const int which = nc / p.d_model;
+            const int rem = nc - which * p.d_model;
+            const int h = rem / p.head_dim;
+            tma_store_3d(tmC, scratch, rem - h * p.head_dim, row_base, which * p.heads + h);
+          } else {
+            tma_store_2d(tmC, scratch, nc, row_base);
+          }
+          bulk_commit();
+        }
+        continue;
+      }
       __syncwarp();
       const uint32_t k = lane & 3;
       const int col = nc + 8 * (int)k;
@@ -523,7 +574,8 @@ struct PairCfg {
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256, EPI), 1)
     gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                             const __grid_constant__ CUtensorMap tmB, const GemmKernelParams p) {
+                             const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmC, const GemmKernelParams p) {
   using Cfg = PairCfg;
   constexpr int S = Cfg::kStages;
   constexpr int BN = Cfg::kBN;
@@ -533,11 +585,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256
                                              ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+  // epilogue scratch (1024-byte aligned: the bulk stores read it in the
+  // 64-byte swizzle), then the barriers
+  const uint32_t scratch_base = smem_u32(sB + S * Cfg::kBBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes + kEpiScratchBytes);
   // bars: full[S] (leader's used), empty[S], tfull[2], tempty[2] (leader's used), final
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const uint32_t scratch_base = smem_u32(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = warp_idx();
   const uint32_t lane = lane_id();
@@ -670,7 +724,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256
       const int n0 = (t % n_tiles) * BN;
       if (!epilogue_tile<BN, EPI, kEpiWarps>(p, tmem_base + (uint32_t)(acc * BN), m0, n0, rows, quarter,
                                              slice, lane, tfull_bar(acc), acc_phase, abort_flag,
-                                             scratch_base + (uint32_t)(warp - 2) * (kEpiScratchBytes / kEpiWarps)))
+                                             scratch_base + (uint32_t)(warp - 2) * (kEpiScratchBytes / kEpiWarps),
+                                             &tmC))
         break;
       tc_fence_before();
       __syncwarp();
@@ -680,6 +735,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads_for(256
         acc_phase ^= 1;
       }
     }
+    if (lane == 0) bulk_wait_all();  // this warp's bulk stores have landed
   }
 
   __syncwarp();
@@ -708,10 +764,10 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// fp16 tensor map of rank 2..5 with a 128-byte swizzle.  dims/strides are in
+// fp16 tensor map of rank 2..5 with the given swizzle.  dims/strides are in
 // elements, innermost first; strides has rank-1 entries (dims 1..rank-1).
-int make_tmap_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                  const uint64_t* strides_elems, const uint32_t* box) {
+static int make_tmap_f16_sw(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                            const uint64_t* strides_elems, const uint32_t* box, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return set_error(TJ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t gdim[5];
@@ -726,12 +782,18 @@ int make_tmap_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* 
   for (int i = 0; i + 1 < rank; ++i) gstride[i] = strides_elems[i] * 2;
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
                   gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(TJ_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d) rank=%d", (int)r,
                      rank);
   return TJ_OK;
+}
+
+// fp16 tensor map of rank 2..5 with a 128-byte swizzle (the operand tiles).
+int make_tmap_f16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides_elems, const uint32_t* box) {
+  return make_tmap_f16_sw(map, base, rank, dims, strides_elems, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <int BN, int EPI>
@@ -802,6 +864,16 @@ static int pair_clusters() {
   return cached;
 }
 
+// TJ_GEMM_TMA_STORE=0 keeps the fp16 epilogues on st.global (for A/B timing).
+static bool gemm_tma_store_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("TJ_GEMM_TMA_STORE");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on != 0;
+}
+
 static bool pair_gemm_enabled() {
   static int on = -1;
   if (on < 0) {
@@ -825,8 +897,30 @@ static int launch_gemm_pair(const GemmArgs& a, const GemmKernelParams& kp, int c
   uint32_t bb[2] = {kBK, (uint32_t)(PairCfg::kBN / 2)};
   rc = make_tmap_f16(&tb, a.w16, 2, db, sb, bb);
   if (rc) return rc;
+  // fp16 outputs in whole 32 x 32 blocks leave through bulk tensor stores: the
+  // QKV head-major layout when heads are not padded (head_dim = 64/128/256),
+  // the plain [rows][ld_out] layout when N is a multiple of 32.
+  GemmKernelParams kq = kp;
+  CUtensorMap tc = ta;  // unused unless kq.tma_store
+  kq.tma_store = 0;
+  if (EPI == kEpiQkvHeadMajor && kp.head_dim == kp.head_pad) {
+    uint64_t dc[3] = {(uint64_t)kp.head_pad, (uint64_t)a.rows_max, (uint64_t)(3 * kp.heads)};
+    uint64_t sc[2] = {(uint64_t)kp.head_pad, (uint64_t)kp.head_pad * (uint64_t)a.rows_max};
+    uint32_t bc[3] = {32, 32, 1};
+    rc = make_tmap_f16_sw(&tc, a.out, 3, dc, sc, bc, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+    kq.tma_store = 1;
+  } else if ((EPI == kEpiBiasF16 || EPI == kEpiGeluF16) && a.N % 32 == 0) {
+    uint64_t dc[2] = {(uint64_t)a.N, (uint64_t)a.rows_max};
+    uint64_t sc[1] = {(uint64_t)a.ld_out};
+    uint32_t bc[2] = {32, 32};
+    rc = make_tmap_f16_sw(&tc, a.out, 2, dc, sc, bc, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+    kq.tma_store = 1;
+  }
+  if (!gemm_tma_store_enabled()) kq.tma_store = 0;
   cudaError_t e = launch_pdl(gemm_tcgen05_pair_kernel<EPI>, dim3(2 * clusters),
-                             dim3(gemm_threads_for(256, EPI)), PairCfg::kSmemBytes, stream, ta, tb, kp);
+                             dim3(gemm_threads_for(256, EPI)), PairCfg::kSmemBytes, stream, ta, tb, tc, kq);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TJ_ERR_CUDA, "gemm pair launch: %s", cudaGetErrorString(e));
   return TJ_OK;
