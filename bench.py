@@ -972,8 +972,9 @@ def main():
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="batch")
     ap.add_argument("--micro-batches", type=int, default=0,
                     help="micro-batches per rank in the split-batch gather (0 = 2 up to 2 GPUs, 4 above)")
-    ap.add_argument("--gather-transport", choices=("kernel", "copy_engine"), default="copy_engine",
-                    help="how the output gather moves rows over NVLink")
+    ap.add_argument("--gather-transport", choices=("copy_engine", "kernel", "nccl"), default="copy_engine",
+                    help="how the output gather moves rows over NVLink: the copy engines (default), "
+                         "the push kernel or NCCL point-to-point")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",

@@ -119,6 +119,61 @@ def gather_segments(assignment: Sequence[Sequence[int]], rank: int, group: Tuple
     return out
 
 
+def p2p_step_plan(assignment: Sequence[Sequence[int]], rank: int, step: int, micro_batches: int,
+                  seq_len: int, valid_lengths: Optional[Sequence[int]]):
+    """Point-to-point transfers of micro-batch step `step` of the NCCL gather,
+    the same on every rank: step k is the k-th range of
+    micro_batch_ranges(len(assignment[r]), micro_batches) on each rank r (empty
+    when r has fewer).  Returns (local_range, sends, recvs, keeps):
+      local_range  this rank's [j0, j1) of the step (None when empty);
+      sends        (peer, local row j - j0 of the micro-batch, rows) per peer,
+                   peers in rank order and, per peer, samples in local order;
+      recvs        (peer, sample b of the batch, rows), the matching order;
+      keeps        (local row, sample b, rows): this rank's own samples.
+    rows = the sample's valid rows (right-padded masks) or seq_len; samples
+    with no rows are skipped on both sides."""
+    world = len(assignment)
+
+    def step_range(r):
+        rs = micro_batch_ranges(len(assignment[r]), micro_batches)
+        return rs[step] if step < len(rs) else None
+
+    def rows(b):
+        return seq_len if valid_lengths is None else int(valid_lengths[b])
+
+    mine = step_range(rank)
+    sends, recvs, keeps = [], [], []
+    if mine is not None:
+        j0, j1 = mine
+        for j in range(j0, j1):
+            b = assignment[rank][j]
+            if rows(b) > 0:
+                keeps.append((j - j0, b, rows(b)))
+        for d in range(world):
+            if d == rank:
+                continue
+            for j in range(j0, j1):
+                b = assignment[rank][j]
+                if rows(b) > 0:
+                    sends.append((d, j - j0, rows(b)))
+    for src in range(world):
+        if src == rank:
+            continue
+        theirs = step_range(src)
+        if theirs is None:
+            continue
+        for j in range(theirs[0], theirs[1]):
+            b = assignment[src][j]
+            if rows(b) > 0:
+                recvs.append((src, b, rows(b)))
+    return mine, sends, recvs, keeps
+
+
+def p2p_steps(assignment: Sequence[Sequence[int]], micro_batches: int) -> int:
+    """Micro-batch steps of the NCCL gather: the most any rank has."""
+    return max((len(micro_batch_ranges(len(a), micro_batches)) for a in assignment), default=0)
+
+
 def zero_fill_segments(valid_lengths: Sequence[int], seq_len: int, row_bytes: int) -> List[Tuple[int, int]]:
     """(byte offset, bytes) of every sample's padded tail in the [B, S, D]
     output of a right-padded batch: the rows no rank sends."""
@@ -152,13 +207,22 @@ class BatchShardedEncoder:
     forward(..., gather=True) also gathers the [B, S, D] output of the whole
     batch on every rank.  The samples run in micro-batches; as soon as one
     micro-batch is finished, the valid rows of its samples go into every
-    rank's output buffer over NVLink (peer mappings; no padded rows on the
-    link) while the next micro-batch computes: by the copy engines (default,
-    one stream per destination) or by one push kernel on a high-priority side
-    stream (transport="kernel", tj_push_segments; measured slower on B200s).
-    Each rank zero-fills the padded rows of its own buffer, and an all-reduce
-    of one element on the current stream, after this rank's last push, is the
-    barrier after which every rank's buffer is complete.
+    rank's output buffer over NVLink (no padded rows on the link) while the
+    next micro-batch computes.  Transports:
+      "copy_engine" (default): copy-engine pushes into the peers' buffers
+          (CUDA IPC peer mappings, one stream per destination);
+      "kernel": one push kernel on a high-priority side stream
+          (tj_push_segments);
+      "nccl": NCCL point-to-point sends of each finished sample's valid rows
+          to every peer, received straight into the peer's output rows
+          (dist.batch_isend_irecv per micro-batch, on NCCL's stream, so the
+          next micro-batch computes meanwhile); each rank waits for its own
+          receives.  Measured on two B200s at B32 S4096: 26 M tokens/s with
+          2 micro-batches and 48 M with 4, against 56 M for the copy engines.
+    With the two push transports an all-reduce of one element on the current
+    stream, after this rank's last push, is the barrier after which every
+    rank's buffer is complete.  Each rank zero-fills the padded rows of its
+    own buffer.
 
     The gathered output is one of `buffers` persistent buffers used in turn:
     the output of call i stays intact until this rank's current stream
@@ -180,8 +244,8 @@ class BatchShardedEncoder:
         # measured on B200s (B32 S4096): 2 micro-batches best at 2 GPUs, 4 from 4 GPUs up
         self.micro_batches = max(1, int(micro_batches)) if micro_batches else (2 if self.world <= 2 else 4)
         self.push_blocks = int(push_blocks)
-        if transport not in ("kernel", "copy_engine"):
-            raise ValueError("transport must be 'kernel' or 'copy_engine'")
+        if transport not in ("nccl", "kernel", "copy_engine"):
+            raise ValueError("transport must be 'nccl', 'kernel' or 'copy_engine'")
         self.transport = transport
         if buffers < 2:
             raise ValueError("the gather needs at least two output buffers")
@@ -233,6 +297,10 @@ class BatchShardedEncoder:
             return self._exchange
         self.close()
         bufs = [torch.empty(B, S, D, dtype=torch.float32, device=device) for _ in range(self.buffers)]
+        if self.transport == "nccl":  # no peer mappings: NCCL moves the rows
+            self._exchange = _Exchange(key, bufs, None, [], [], None)
+            self._turn = 0
+            return self._exchange
         mine = [_lib.ipc_export(b.data_ptr()) for b in bufs]
         every = [None] * self.world
         dist.all_gather_object(every, mine, group=self.group)
@@ -270,10 +338,11 @@ class BatchShardedEncoder:
 
         for s in ex.streams:
             s.synchronize()
-        torch.cuda.current_stream(ex.flag.device).synchronize()
+        dev = ex.bufs[0].device
+        torch.cuda.current_stream(dev).synchronize()
         for base in ex.mapped:
             _lib.ipc_close(base)
-        dist.barrier(group=self.group, device_ids=[ex.flag.device.index])
+        dist.barrier(group=self.group, device_ids=[dev.index])
         self._exchange = None
 
     def _gather_forward(self, x_local, mask_local, assignment, valid_lengths):
@@ -296,9 +365,11 @@ class BatchShardedEncoder:
         row_bytes = D * 4
         compute = torch.cuda.current_stream(dev)
         if valid_lengths is not None:
-            base = ex.ptrs[self.rank][buf]
+            base = ex.bufs[buf].data_ptr()
             _lib.copy_segments([(base + off, 0, n) for off, n in zero_fill_segments(valid_lengths, S, row_bytes)],
                                compute.cuda_stream)
+        if self.transport == "nccl":
+            return self._gather_nccl(x_local, mask_local, assignment, valid_lengths, ex.bufs[buf])
         push = ex.streams[0]
         dsts = [ex.ptrs[d][buf] for d in range(self.world)]
         for j0, j1 in micro_batch_ranges(n_local, self.micro_batches):
@@ -323,6 +394,41 @@ class BatchShardedEncoder:
         # every rank's pushes (ordered before it on that rank's stream) landed.
         dist.all_reduce(ex.flag, group=self.group)
         return ex.bufs[buf]
+
+    def _gather_nccl(self, x_local, mask_local, assignment, valid_lengths, out_all):
+        """Micro-batch k on every rank, then one batch_isend_irecv per step:
+        the step's valid rows to every peer, the peers' step-k rows straight
+        into out_all; NCCL runs them on its own stream after the step's
+        forward, while the next step computes.  The current stream waits for
+        this rank's receives at the end."""
+        import torch.distributed as dist
+
+        S = out_all.shape[1]
+        works, keep_alive = [], []
+        group_ranks = None if self.group is None else dist.get_process_group_ranks(self.group)
+
+        def peer(r):  # group rank -> global rank for P2POp
+            return r if group_ranks is None else group_ranks[r]
+
+        for k in range(p2p_steps(assignment, self.micro_batches)):
+            mine, sends, recvs, keeps = p2p_step_plan(assignment, self.rank, k, self.micro_batches, S,
+                                                      valid_lengths)
+            ops = []
+            if mine is not None:
+                j0, j1 = mine
+                out = self.model(x_local[j0:j1], None if mask_local is None else mask_local[j0:j1])
+                keep_alive.append(out)
+                for jl, b, n in keeps:
+                    out_all[b, :n].copy_(out[jl, :n])
+                for d, jl, n in sends:
+                    ops.append(dist.P2POp(dist.isend, out[jl, :n], peer(d), group=self.group))
+            for src, b, n in recvs:
+                ops.append(dist.P2POp(dist.irecv, out_all[b, :n], peer(src), group=self.group))
+            if ops:
+                works.extend(dist.batch_isend_irecv(ops))
+        for w in works:
+            w.wait()
+        return out_all
 
 
 def segment_metadata(counts: torch.Tensor, rank: int, causal: bool):

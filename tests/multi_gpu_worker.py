@@ -2,9 +2,10 @@
 
 Checks, on N GPUs over NCCL:
   * batch sharding: each rank runs its balanced range of the batch; the
-    gathered output (copy engines over NVLink, or the push kernel; valid rows only
-    for right-padded masks, whole samples otherwise; 1-3 micro-batches) is
-    bit-identical to the whole batch on one GPU;
+    gathered output (NCCL point-to-point, the copy engines over NVLink, or the
+    push kernel; valid rows only for right-padded masks, whole samples
+    otherwise; 1-3 micro-batches) is bit-identical to the whole batch on one
+    GPU;
   * context parallelism: one sequence split into valid-token balanced chunks,
     K/V exchanged every layer (copy engines overlapped with attention over
     the own keys, then a merged launch over the others; and the plain
@@ -80,12 +81,15 @@ def main() -> int:
                                  valid_lengths=lengths)
                 if not torch.equal(out, full):
                     failures.append(f"valid-row gather (micro-batches {mb}, call {rep}) differs from one GPU")
-        # the push-kernel transport of the same gather
-        pk = sharding.BatchShardedEncoder(model, micro_batches=2, transport="kernel")
-        out = pk.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign, valid_lengths=lengths)
-        if not torch.equal(out, full):
-            failures.append("push-kernel gather differs from one GPU")
-        pk.close()
+        # the other transports of the same gather (push kernel, NCCL point-to-point)
+        for transport in ("kernel", "nccl"):
+            pk = sharding.BatchShardedEncoder(model, micro_batches=2, transport=transport)
+            for rep in range(2):
+                out = pk.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign,
+                                 valid_lengths=lengths)
+                if not torch.equal(out, full):
+                    failures.append(f"{transport} gather (call {rep}) differs from one GPU")
+            pk.close()
         # a non-prefix mask: whole samples are copied
         mask2 = mask.clone()
         mask2[:, 1::3] = False

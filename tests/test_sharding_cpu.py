@@ -243,3 +243,101 @@ def test_split_attention_merge_formula():
         c = 0.0 if float(lse1) == float("-inf") else 2.0 ** (float(lse1) - M)
         merged = (O2 * a + o1 * c) / (l2 * a + c)
         torch.testing.assert_close(merged, full, rtol=1e-12, atol=1e-12)
+
+
+def _p2p_gather_rank(rank, world, port, micro, prefix, result_q):
+    """One gloo rank of the point-to-point gather: the plan of p2p_step_plan
+    run with real sends and receives (dist.batch_isend_irecv, as the NCCL
+    transport issues them) over CPU tensors standing in for each micro-batch's
+    output."""
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import __graft_entry__
+
+        __graft_entry__.load_package()
+        from techjam_b200 import sharding
+
+        g = torch.Generator().manual_seed(99 + world + micro)
+        B, S, D = 11, 7, 5
+        lengths = torch.randint(0, S + 1, (B,), generator=g).tolist()
+        full = torch.randn(B, S, D, generator=g)
+        for b, n in enumerate(lengths):
+            full[b, n:] = 0
+        assign = sharding.balanced_assignment(lengths, world, 64, 256)
+        valid = lengths if prefix else None
+        out_all = torch.full((B, S, D), float("nan"))
+        if prefix:  # the receiver's zero fill of padded rows
+            for b, n in enumerate(lengths):
+                out_all[b, n:] = 0
+        mine = assign[rank]
+        steps = sharding.p2p_steps(assign, micro)
+        for k in range(steps):
+            rng, sends, recvs, keeps = sharding.p2p_step_plan(assign, rank, k, micro, S, valid)
+            ops = []
+            if rng is not None:
+                j0, j1 = rng
+                out = full[torch.tensor(mine[j0:j1], dtype=torch.int64)].contiguous()  # "the forward"
+                for jl, b, n in keeps:
+                    out_all[b, :n].copy_(out[jl, :n])
+                for d, jl, n in sends:
+                    ops.append(dist.P2POp(dist.isend, out[jl, :n].contiguous(), d))
+            recv_bufs = []
+            for src, b, n in recvs:
+                t = torch.empty(n, D)
+                recv_bufs.append((b, n, t))
+                ops.append(dist.P2POp(dist.irecv, t, src))
+            if ops:
+                for w in dist.batch_isend_irecv(ops):
+                    w.wait()
+            for b, n, t in recv_bufs:
+                out_all[b, :n] = t
+        ok = torch.equal(out_all, full)
+        result_q.put((rank, ok, None))
+    except Exception as e:  # report to the parent instead of hanging it
+        result_q.put((rank, False, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,micro", [(2, 2), (3, 4)])
+@pytest.mark.parametrize("prefix", [True, False])
+def test_p2p_gather_plan_gloo_ranks(pkg, world, micro, prefix):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_p2p_gather_rank, args=(r, world, port, micro, prefix, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, exc in sorted(results):
+        assert exc is None, f"rank {rank}: {exc}"
+        assert ok, f"rank {rank}: gathered output differs"
+
+
+def test_p2p_plan_matches_pairwise(pkg):
+    """Sender and receiver enumerate the same transfers in the same order, for
+    every ordered rank pair and step (NCCL matches point-to-point operations
+    between two ranks in posting order)."""
+    from techjam_b200 import sharding
+
+    g = torch.Generator().manual_seed(5)
+    for world in (2, 3, 8):
+        for B in (1, 6, 13, 32):
+            lengths = torch.randint(0, 50, (B,), generator=g).tolist()
+            assign = sharding.balanced_assignment(lengths, world, 64, 256)
+            for micro in (1, 2, 4):
+                for k in range(sharding.p2p_steps(assign, micro)):
+                    plans = [sharding.p2p_step_plan(assign, r, k, micro, 50, lengths) for r in range(world)]
+                    for s in range(world):
+                        for d in range(world):
+                            if s == d:
+                                continue
+                            sent = [n for dd, _, n in plans[s][1] if dd == d]
+                            got = [n for ss, _, n in plans[d][2] if ss == s]
+                            assert sent == got, (world, B, micro, k, s, d)
