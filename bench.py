@@ -22,6 +22,8 @@ max over ranks of the CUDA-event time of the K timed steps.
 The same JSON line nests, measured in the same run at the same N:
   dense_b8_s2048     the single-GPU dense layer (B=8 S=2048, lengths U[S/2,S])
                      per rank (weak scaling), with its attention roofline;
+  short_b64_s128     the short-sequence heavy-padding layer (B=64 S=128
+                     d_model=768 H=12 FFN=3072, lengths U[1,S]) per rank;
   context_parallel   one sequence of S=131072 (lengths U[0.9S, S]) over the
                      N ranks (context parallel; the plain model at N=1), with
                      peak memory per GPU;
@@ -348,10 +350,13 @@ def run_ours(args, world, rank, local):
             if args.workload == "batch" and not args.no_extras:
                 dense = measure_headline(pkg, argparse.Namespace(**{**vars(args), "workload": "dense"}), world,
                                          rank, local, device, nested=True)
+                short = measure_headline(pkg, argparse.Namespace(**{**vars(args), "workload": "short"}), world,
+                                         rank, local, device, nested=True)
                 cp = measure_long(pkg, args, world, rank, local, device, headline=False)
                 shapes = measure_official_shapes(pkg, args, device) if world == 1 else None
                 if rank == 0:
                     line["dense_b8_s2048"] = dense
+                    line["short_b64_s128"] = short
                     line["context_parallel"] = cp
                     line["official_shapes"] = shapes
     finally:
