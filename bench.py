@@ -376,7 +376,7 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
     B, S = cfg.batch_size, cfg.seq_len
     model = case.model(pkg, device)
     encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches,
-                                           transport=args.gather_transport)
+                                           transport=args.gather_transport, copy_streams=args.copy_streams)
     gather = case.split and world > 1
     lengths = case.lengths if case.right_padded else None
     mask_local = case.mask_local.to(device)
@@ -448,7 +448,9 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
         "parallelism": (f"batch split x{world}: {B // world} samples per GPU balanced by work; the step includes "
                         "the output gather (valid rows pushed over NVLink into every "
                         f"GPU's [B,S,D] output, {encoder.micro_batches} micro-batches overlapping it, "
-                        f"transport: {encoder.transport})"
+                        f"transport: {encoder.transport}"
+                        + (f", {encoder.copy_streams} streams per destination)" if encoder.transport == "copy_engine"
+                           else ")")
                         if gather else
                         (f"batch split x{world}" if case.split else
                          f"x{world}: each GPU runs its own batch of {B} (weak scaling, no collective)")),
@@ -622,7 +624,7 @@ def measure_e2e(case, model, device, args, world, gather, lengths):
     # three exchange buffers: the download of step i-3 is the last reader of
     # the buffer the gather of step i writes, and it completes before step i-1
     encoder = sharding.BatchShardedEncoder(model, micro_batches=args.micro_batches, buffers=3,
-                                           transport=args.gather_transport)
+                                           transport=args.gather_transport, copy_streams=args.copy_streams)
     mine = torch.tensor(case.mine, dtype=torch.int64, device=device)
     x_host = [x_cpu.clone().pin_memory() for _ in range(nbuf)]
     m_host = mask_cpu.pin_memory()
@@ -980,6 +982,8 @@ def main():
     ap.add_argument("--gather-transport", choices=("copy_engine", "kernel", "nccl"), default="copy_engine",
                     help="how the output gather moves rows over NVLink: the copy engines (default), "
                          "the push kernel or NCCL point-to-point")
+    ap.add_argument("--copy-streams", type=int, default=1,
+                    help="copy-engine gather: streams per destination, each pushing an equal share")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",

@@ -169,6 +169,26 @@ def p2p_step_plan(assignment: Sequence[Sequence[int]], rank: int, step: int, mic
     return mine, sends, recvs, keeps
 
 
+def split_segments(segs: Sequence[Tuple[int, int, int]], parts: int, row_bytes: int) -> List[List[Tuple[int, int, int]]]:
+    """Deals copies (dst offset, src offset, bytes) to `parts` queues of
+    about equal bytes, cutting a copy at whole rows where it straddles two
+    queues; concatenated in queue order they cover the same bytes."""
+    parts = max(1, int(parts))
+    total = sum(n for _, _, n in segs)
+    share = -(-total // parts)
+    share = -(-share // row_bytes) * row_bytes if row_bytes > 0 else share
+    out: List[List[Tuple[int, int, int]]] = [[] for _ in range(parts)]
+    q, room = 0, share
+    for do, so, n in segs:
+        while n > 0:
+            if room == 0 and q + 1 < parts:
+                q, room = q + 1, share
+            take = n if q + 1 == parts else min(n, room)
+            out[q].append((do, so, take))
+            do, so, n, room = do + take, so + take, n - take, room - take
+    return out
+
+
 def p2p_steps(assignment: Sequence[Sequence[int]], micro_batches: int) -> int:
     """Micro-batch steps of the NCCL gather: the most any rank has."""
     return max((len(micro_batch_ranges(len(a), micro_batches)) for a in assignment), default=0)
@@ -232,7 +252,7 @@ class BatchShardedEncoder:
     process group goes away."""
 
     def __init__(self, model, group=None, micro_batches: Optional[int] = None, buffers: int = 2,
-                 push_blocks: int = 64, transport: str = "copy_engine") -> None:
+                 push_blocks: int = 64, transport: str = "copy_engine", copy_streams: int = 1) -> None:
         import torch.distributed as dist
 
         self.model = model
@@ -247,6 +267,9 @@ class BatchShardedEncoder:
         if transport not in ("nccl", "kernel", "copy_engine"):
             raise ValueError("transport must be 'nccl', 'kernel' or 'copy_engine'")
         self.transport = transport
+        # copy engines: streams per destination, each pushing an equal share of
+        # every micro-batch's rows (so several engines can serve one peer)
+        self.copy_streams = max(1, int(copy_streams))
         if buffers < 2:
             raise ValueError("the gather needs at least two output buffers")
         self.buffers = int(buffers)
@@ -319,7 +342,7 @@ class BatchShardedEncoder:
         # kernel: one high-priority stream, its push kernel's CTAs scheduled
         # ahead of the next micro-batch's waiting CTAs; copy engines: one
         # stream per destination, so the copies run on several engines
-        n_streams = 1 if self.transport == "kernel" else self.world
+        n_streams = 1 if self.transport == "kernel" else self.world * self.copy_streams
         streams = [torch.cuda.Stream(device, priority=-1) for _ in range(n_streams)]
         flag = torch.zeros(1, dtype=torch.int32, device=device)
         self._exchange = _Exchange(key, bufs, ptrs, list(mapped.values()), streams, flag)
@@ -384,10 +407,16 @@ class BatchShardedEncoder:
                                    blocks=self.push_blocks)
                 out.record_stream(push)
             else:
-                for d, stream in enumerate(ex.streams):
-                    stream.wait_event(done)
-                    _lib.copy_segments([(dsts[d] + do, src + so, n) for do, so, n in segs], stream.cuda_stream)
-                    out.record_stream(stream)
+                k = self.copy_streams
+                shares = split_segments(segs, k, row_bytes)
+                for d in range(self.world):
+                    for i in range(k):
+                        stream = ex.streams[d * k + i]
+                        stream.wait_event(done)
+                        if shares[i]:
+                            _lib.copy_segments([(dsts[d] + do, src + so, n) for do, so, n in shares[i]],
+                                               stream.cuda_stream)
+                        out.record_stream(stream)
         for stream in ex.streams:
             compute.wait_stream(stream)
         # Completes on a rank only after every rank has reached it, i.e. after

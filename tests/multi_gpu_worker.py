@@ -81,14 +81,15 @@ def main() -> int:
                                  valid_lengths=lengths)
                 if not torch.equal(out, full):
                     failures.append(f"valid-row gather (micro-batches {mb}, call {rep}) differs from one GPU")
-        # the other transports of the same gather (push kernel, NCCL point-to-point)
-        for transport in ("kernel", "nccl"):
-            pk = sharding.BatchShardedEncoder(model, micro_batches=2, transport=transport)
+        # the other transports of the same gather (push kernel, NCCL point-to-point,
+        # copy engines with three streams per destination)
+        for transport, k in (("kernel", 1), ("nccl", 1), ("copy_engine", 3)):
+            pk = sharding.BatchShardedEncoder(model, micro_batches=2, transport=transport, copy_streams=k)
             for rep in range(2):
                 out = pk.forward(x[mine].to(dev), mask[mine].to(dev), gather=True, assignment=assign,
                                  valid_lengths=lengths)
                 if not torch.equal(out, full):
-                    failures.append(f"{transport} gather (call {rep}) differs from one GPU")
+                    failures.append(f"{transport} gather ({k} streams, call {rep}) differs from one GPU")
             pk.close()
         # a non-prefix mask: whole samples are copied
         mask2 = mask.clone()

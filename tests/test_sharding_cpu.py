@@ -341,3 +341,30 @@ def test_p2p_plan_matches_pairwise(pkg):
                             sent = [n for dd, _, n in plans[s][1] if dd == d]
                             got = [n for ss, _, n in plans[d][2] if ss == s]
                             assert sent == got, (world, B, micro, k, s, d)
+
+
+def test_split_segments_covers_the_same_rows(pkg):
+    """The copy-engine gather's per-stream shares: every byte once, in order,
+    cut only at whole rows, about equal shares."""
+    from techjam_b200 import sharding
+
+    g = torch.Generator().manual_seed(3)
+    for row in (4, 12, 4096):
+        for _ in range(200):
+            segs, off = [], 0
+            for _ in range(int(torch.randint(0, 6, (1,), generator=g))):
+                n = row * int(torch.randint(1, 60, (1,), generator=g))
+                segs.append((3 * off + 7, off, n))
+                off += n
+            for parts in (1, 2, 3, 4, 7):
+                shares = sharding.split_segments(segs, parts, row)
+                assert len(shares) == parts
+                flat = [c for s in shares for c in s]
+                assert all(n > 0 and n % row == 0 for _, _, n in flat)
+                want = [(do + i, so + i) for do, so, n in segs for i in range(0, n, row)]
+                got = [(do + i, so + i) for do, so, n in flat for i in range(0, n, row)]
+                assert got == want
+                total = sum(n for _, _, n in segs)
+                if total:
+                    cap = -(-total // parts)
+                    assert max(sum(n for _, _, n in s) for s in shares) <= cap + row
