@@ -449,8 +449,8 @@ def measure_headline(pkg, args, world, rank, local, device, nested=False):
                         "the output gather (valid rows pushed over NVLink into every "
                         f"GPU's [B,S,D] output, {encoder.micro_batches} micro-batches overlapping it, "
                         f"transport: {encoder.transport}"
-                        + (f", {encoder.copy_streams} streams per destination)" if encoder.transport == "copy_engine"
-                           else ")")
+                        + (f", {encoder.copy_streams} stream{'s' if encoder.copy_streams > 1 else ''} per "
+                           "destination)" if encoder.transport == "copy_engine" else ")")
                         if gather else
                         (f"batch split x{world}" if case.split else
                          f"x{world}: each GPU runs its own batch of {B} (weak scaling, no collective)")),
